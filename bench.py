@@ -1,0 +1,373 @@
+"""Benchmark: BCJR forward+backward state-transitions/sec on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c3|c5]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, NCCL)
+
+Workload (synthetic, seeded): L=16, k=2, V=1, N=256 steps,
+T=0.5, codebook randn(65536) (seed 0), weights randn drawn after the codebook.
+* c2 (default): one 1024x1024 weight = 4,096 sequences per GPU (weak scaling:
+  every rank quantizes its own matrix; the soft matrices are all-gathered
+  over NCCL when N > 1).
+* c3: the Llama-3.2-1B-shaped layer (237,568 sequences, per-row scale
+  U[0.5,2]) sharded across the N ranks (strong scaling), soft weights
+  all-gathered.
+* c5: the OLMoE-shaped MoE layer (1,572,864 sequences), experts sharded
+  8 per GPU at N=8 (strong scaling).
+
+One step = forward (soft) + backward (d_seq for an upstream gradient of ones)
+of every local sequence (+ the all-gather when N > 1).  One transition = one
+trellis edge: B * N * 2^L * 2^kV per step.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "BCJR fwd+bwd state-transitions/sec (L=16,k=2) at 1/2/4/8 B200; % MUFU roofline"
+UNIT = "transitions/s"
+L, K_BITS, V, NSTEP, TEMP = 16, 2, 1, 256, 0.5
+EDGES_PER_SEQ = NSTEP * (1 << L) * (1 << (K_BITS * V))
+STATE_STEPS_PER_SEQ = NSTEP * (1 << L)
+# Algorithmic MUFU (ex2/lg2/rcp) per state-step, forward call and backward
+# call, at kV = 2: alpha LSE 5/4 + beta LSE 5/4 + marginal exp 1 = 3.5 for the
+# forward; the same recompute plus 2/2^b softmax normalisers = 4.0 for the
+# backward (7.5 per fwd+bwd state-step).
+MUFU_FWD, MUFU_BWD = 3.5, 4.0
+MUFU_PER_SM_CLK = 16
+L2_BYTES = 126 * 1024 * 1024
+
+
+def llama_layer_shapes():
+    # q, k, v, o, gate, up, down (out x in), Llama-3.2-1B
+    return [(2048, 2048), (512, 2048), (512, 2048), (2048, 2048),
+            (8192, 2048), (8192, 2048), (2048, 8192)]
+
+
+def olmoe_layer_shapes():
+    return [(1024, 2048), (1024, 2048), (2048, 1024)] * 64
+
+
+def tile(W, Tx=16, Ty=16):
+    """Reference tile order (src/qat/ste.py:138-149): sequence j*(m/16)+i holds
+    the row-major 16x16 block at rows 16i.., cols 16j.."""
+    m, n = W.shape
+    return W.view(m, n // Ty, Ty).permute(1, 0, 2).reshape((m // Tx) * (n // Ty), Tx * Ty)
+
+
+def make_inputs(config, rank, world):
+    """Codebook (65536, 1) and this rank's sequences (B_local, 256, 1), on CPU."""
+    g = torch.Generator().manual_seed(0)
+    cb = torch.randn(1 << L, 1, generator=g)
+    if config == "c2":
+        gw = torch.Generator().manual_seed(1000 + rank) if rank else g
+        w = torch.randn(4096, NSTEP, 1, generator=gw)
+        return cb, w, 4096 * world
+    shapes = llama_layer_shapes() if config == "c3" else olmoe_layer_shapes()
+    total = sum((m // 16) * (n // 16) for m, n in shapes)
+    lo, hi = rank * total // world, (rank + 1) * total // world
+    seqs, off = [], 0
+    gs = torch.Generator().manual_seed(7)
+    for idx, (m, n) in enumerate(shapes):
+        cnt = (m // 16) * (n // 16)
+        if off + cnt > lo and off < hi:
+            gm = torch.Generator().manual_seed(100 + idx)
+            if config == "c3":
+                scale = torch.empty(m, 1).uniform_(0.5, 2.0, generator=gm)
+            else:
+                scale = torch.empty(1, 1).uniform_(0.5, 2.0, generator=gm)
+            W = torch.randn(m, n, generator=gm) * scale
+            t = tile(W)
+            a, b_ = max(lo, off) - off, min(hi, off + cnt) - off
+            seqs.append(t[a:b_])
+        off += cnt
+    w = torch.cat(seqs).view(-1, NSTEP, 1).contiguous()
+    return cb, w, total
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, r[5:9]):
+                if val.lower() in ("active", "1"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference(args, rank):
+    """The reference's eager torch BCJR (restated in oracle/torch_port.py) on
+    the host's CPU cores: one forward + backward of a bounded sample of the
+    same workload per step."""
+    from oracle import torch_port
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cb, w, _ = make_inputs("c2" if args.config == "c2" else args.config, 0, 1)
+    nseq = args.cpu_sample_seqs
+    sample = w[:nseq]
+    for _ in range(args.warmup if args.impl == "reference" else 0):
+        torch_port.fwd_bwd(sample, cb, TEMP, L, K_BITS, V, chunk=8)
+    t0 = time.perf_counter()
+    steps = args.steps if args.impl == "reference" else 1
+    for _ in range(steps):
+        torch_port.fwd_bwd(sample, cb, TEMP, L, K_BITS, V, chunk=8)
+    dt = (time.perf_counter() - t0) / steps
+    value = nseq * EDGES_PER_SEQ / dt
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{nseq} sequence(s) of {args.config} (L=16, N=256), fwd + bwd with "
+                      f"grad=ones, chunk 8, torch {torch.__version__} CPU, "
+                      f"{threads} threads, {dt:.2f} s per step"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5"])
+    ap.add_argument("--cpu-sample-seqs", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        ref = cpu_reference(args, rank)
+        line = {"metric": METRIC, "value": ref["value"], "unit": UNIT, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": args.cpu_sample_seqs * EDGES_PER_SEQ / ref["value"] * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic (seeded randn, BASELINE configs)",
+                "impl": "reference",
+                "config": {"workload": f"{args.config}: L=16 k=2 V=1 N=256 T=0.5, CPU sample",
+                           "sample_sequences": args.cpu_sample_seqs},
+                "cpu_baseline": ref,
+                "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import quant_2bit_b200 as q
+    from quant_2bit_b200 import _lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+
+    cb_cpu, w_cpu, total_seqs = make_inputs(args.config, rank, world)
+    cb = cb_cpu.to(dev)
+    w = w_cpu.to(dev)
+    Bl = w.shape[0]
+    T = torch.tensor(TEMP, dtype=torch.float32, device=dev)
+    soft = torch.empty((Bl, NSTEP, V), device=dev)
+    logZ = torch.empty((Bl,), device=dev)
+    grad = torch.ones((Bl, NSTEP, V), device=dev)
+    dseq = torch.empty_like(soft)
+    lib = _lib.load()
+    ws_f = _lib.workspace(Bl, NSTEP, L, K_BITS, V, _lib.WS_FORWARD, dev)
+    ws_b = _lib.workspace(Bl, NSTEP, L, K_BITS, V, _lib.WS_BACKWARD, dev)
+    gathered = torch.empty((Bl * world, NSTEP, V), device=dev) if world > 1 else None
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = _lib.stream_ptr(dev)
+
+    def fwd():
+        _lib.check(lib.bcjr_fb_forward(_lib.ptr(w), _lib.ptr(cb), _lib.ptr(T), Bl, NSTEP, L,
+                                       K_BITS, V, _lib.ptr(soft), _lib.ptr(logZ),
+                                       _lib.ptr(ws_f), ws_f.numel(), sp), "forward")
+
+    def bwd():
+        _lib.check(lib.bcjr_fb_backward(_lib.ptr(w), _lib.ptr(cb), _lib.ptr(T), _lib.ptr(soft),
+                                        _lib.ptr(grad), Bl, NSTEP, L, K_BITS, V,
+                                        _lib.ptr(dseq), _lib.ptr(ws_b), ws_b.numel(), sp),
+                   "backward")
+
+    def step(ev=None):
+        if ev:
+            ev[0].record(stream)
+        fwd()
+        if ev:
+            ev[1].record(stream)
+        bwd()
+        if ev:
+            ev[2].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, soft)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    props = torch.cuda.get_device_properties(dev)
+    uuid = getattr(props, "uuid", None)
+    clocks = ClockSampler(f"GPU-{uuid}" if uuid is not None else local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()                     # L2 flush between timed steps (outside the events)
+        step(events[i])
+        events[i][3].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+
+    step_ms = [e[0].elapsed_time(e[3]) for e in events]
+    fwd_ms = [e[0].elapsed_time(e[1]) for e in events]
+    bwd_ms = [e[1].elapsed_time(e[2]) for e in events]
+    t_local = sum(step_ms)
+    t = torch.tensor([t_local], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_max_ms = float(t.item())
+    edges_total = Bl * world * EDGES_PER_SEQ if args.config == "c2" else total_seqs * EDGES_PER_SEQ
+    value = edges_total * args.steps / (t_max_ms / 1e3)
+
+    # e2e: the public autograd API with host buffers, H2D and D2H in the timed region.
+    w_host = w_cpu.pin_memory()
+    soft_host = torch.empty((Bl, NSTEP, V)).pin_memory()
+    dseq_host = torch.empty((Bl, NSTEP, V)).pin_memory()
+
+    def e2e_step():
+        x = w_host.to(dev, non_blocking=True).requires_grad_(True)
+        s, _ = q.bcjr_forward_backward(x, cb, T, L=L, k=K_BITS, V=V)
+        s.sum().backward()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, s.detach())
+        soft_host.copy_(s.detach(), non_blocking=True)
+        dseq_host.copy_(x.grad, non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    e2e_value = edges_total * args.steps / (float(te.item()) / 1e3)
+
+    # roofline of the dominant kernel (MUFU-bound; algorithmic ops per launch)
+    fwd_avg = sum(fwd_ms) / len(fwd_ms)
+    bwd_avg = sum(bwd_ms) / len(bwd_ms)
+    sstep = Bl * STATE_STEPS_PER_SEQ
+    if bwd_avg >= fwd_avg:
+        dom, dom_ms, ops = "backward", bwd_avg, MUFU_BWD * sstep
+    else:
+        dom, dom_ms, ops = "forward", fwd_avg, MUFU_FWD * sstep
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    clk_mhz = clk.get("sm_max_mhz") or 1965.0
+    peak = sms * MUFU_PER_SM_CLK * clk_mhz * 1e6 / 1e9          # Gop/s at max SM clock
+    achieved = ops / (dom_ms / 1e3) / 1e9
+
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_max_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak" if args.config == "c2" else "strong",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded randn codebook and weights, BASELINE configs)",
+            "config": {"workload": {"c2": "config 2: one 1024x1024 weight per GPU",
+                                    "c3": "config 3: Llama-3.2-1B layer, sharded",
+                                    "c5": "config 5: OLMoE MoE layer, sharded"}[args.config]
+                       + " (L=16, k=2, V=1, N=256, T=0.5, fwd+bwd, grad=ones)",
+                       "sequences_per_gpu": Bl, "sequences_total": total_seqs if args.config != "c2" else Bl * world,
+                       "l2": "flushed between timed steps (256 MB write, outside the events)",
+                       "collective": "NCCL all_gather of soft per step" if world > 1 else "none"},
+            "clocks": clk,
+            "gpu_launches": 2 * args.steps,
+            "kernel_ms": {"forward": fwd_avg, "backward": bwd_avg},
+            "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak,
+                         "unit": "Gop/s", "frac": achieved / peak, "traffic": None,
+                         "note": f"algorithmic MUFU ops: {MUFU_FWD}/{MUFU_BWD} per state-step "
+                                 f"(fwd/bwd call), peak = {sms} SMs x 16/clk x {clk_mhz:.0f} MHz"},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": w_host.numel() * 4,
+                    "d2h_bytes_per_step": (soft_host.numel() + dseq_host.numel()) * 4},
+        }
+        if world > 1:
+            result["e2e"]["note"] = "per rank: H2D of its shard, D2H of its soft and d_seq"
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if not args.no_cpu_baseline and world == 1:
+            result["cpu_baseline"] = cpu_reference(args, rank)
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,130 @@
+/*
+ * bcjr_b200 -- C ABI of the B200 (sm_100a) BCJR forward-backward library.
+ *
+ * The library computes sum-product message passing at temperature T over the
+ * QTIP bitshift trellis (2^L states, next state ((s << kV) | c) & (2^L - 1))
+ * with a per-state codebook c(s) in R^V, for B independent sequences of N
+ * steps.  It returns the soft codeword E[c(s_t)] per step and, in the
+ * backward entry point, the gradient of <grad_soft, soft> with respect to the
+ * input sequence.
+ *
+ * All pointers are device pointers (fp32, C-contiguous) unless stated
+ * otherwise.  Every call is asynchronous and ordered on `stream`; no call
+ * synchronises the host or reads T on the host.  The caller owns every
+ * buffer, including the workspace, whose size comes from
+ * bcjr_workspace_bytes().  Calls on the same workspace must not overlap.
+ *
+ * Reference interfaces replaced (Venugopalan2610/quant-2bit):
+ *   src/bcjr/bcjr_monolithic.py:157-243  BcjrForwardBackwardMonolithic
+ *   src/bcjr/forward_backward.py:190-232  bcjr_forward_backward
+ *   src/bcjr/bcjr_triton.py:32-119        the per-step Triton kernels
+ */
+#ifndef BCJR_B200_H
+#define BCJR_B200_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define BCJR_API __attribute__((visibility("default")))
+#else
+#define BCJR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; declared here so that the header needs no
+ * CUDA include.  Pass 0 for the legacy default stream. */
+typedef struct CUstream_st *bcjr_stream_t;
+
+/* Status codes.  0 is success.  The reference raises AssertionError for shape
+ * and dtype problems (forward_backward.py:206-207, bcjr_monolithic.py:162-163);
+ * the Python layer maps BCJR_ERR_BAD_SHAPE back to AssertionError. */
+enum {
+    BCJR_OK = 0,
+    BCJR_ERR_BAD_SHAPE = 1,      /* B, N, L, k, V inconsistent or out of range */
+    BCJR_ERR_UNSUPPORTED = 2,    /* (L, k, V) combination not built           */
+    BCJR_ERR_NULL_POINTER = 3,   /* a required pointer is NULL                */
+    BCJR_ERR_ALIGNMENT = 4,      /* pointer not aligned to its element size   */
+    BCJR_ERR_WORKSPACE = 5,      /* workspace missing or too small            */
+    BCJR_ERR_LAUNCH = 6,         /* CUDA launch or device query failed        */
+    BCJR_ERR_DEVICE = 7,         /* device is not sm_100 or not usable        */
+    BCJR_ERR_TIMEOUT = 8         /* a bounded device-side wait gave up        */
+};
+
+/* Workspace flags for bcjr_workspace_bytes(). */
+enum {
+    BCJR_WS_FORWARD = 1,
+    BCJR_WS_BACKWARD = 2,
+    BCJR_WS_INTERNALS = 4
+};
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+BCJR_API int bcjr_version(void);
+
+/* Static string for a status code. */
+BCJR_API const char *bcjr_status_string(int status);
+
+/* Bytes of device workspace needed by the entry points named in `flags` for
+ * this problem on the current device.  Returns 0 for an invalid or
+ * unsupported shape (bcjr_check_shape() gives the reason).
+ * Replaces the reference's per-call (B,N,S) allocations
+ * (bcjr_monolithic.py:49-56, :83-87, :109-112) with an O(grid) buffer. */
+BCJR_API size_t bcjr_workspace_bytes(int B, int N, int L, int k, int V, int flags);
+
+/* Shape validation without launching anything: BCJR_OK or the error code. */
+BCJR_API int bcjr_check_shape(int B, int N, int L, int k, int V);
+
+/*
+ * Forward: soft[b,t,:] = sum_s P_t(s) c(s)  and  logZ[b] (natural log).
+ *   seq   (B, N, V)   input sequences (the 16x16 weight tiles)
+ *   cb    (2^L, V)    codebook
+ *   T_dev scalar      temperature, device memory (read on the device)
+ *   soft  (B, N, V)   output
+ *   logZ  (B,)        output, may be NULL
+ * Replaces BcjrForwardBackwardMonolithic.forward (bcjr_monolithic.py:160-189)
+ * and the value part of bcjr_forward_backward (forward_backward.py:190-232).
+ */
+BCJR_API int bcjr_fb_forward(const float *seq, const float *cb, const float *T_dev,
+                    int B, int N, int L, int k, int V,
+                    float *soft, float *logZ,
+                    void *ws, size_t ws_bytes, bcjr_stream_t stream);
+
+/*
+ * Backward: d_seq = d <grad_soft, soft> / d seq, the gradient the reference's
+ * analytic backward defines (bcjr_monolithic.py:191-243):
+ *   d_seq[b,u,:] = (2/T) sum_s dl_u(s) (c(s) - seq[b,u,:]),
+ *   dl_u(s) = P_u(s) (E[G | s_u = s] - E[G]),  G = sum_t <grad_soft_t, c(s_t)>.
+ *   soft       (B, N, V)  the forward's output (used to centre G)
+ *   grad_soft  (B, N, V)  upstream gradient
+ *   d_seq      (B, N, V)  output
+ * Replaces BcjrForwardBackwardMonolithic.backward and the Triton
+ * _alpha_step_bwd_kernel scatter (bcjr_triton.py:75-119).
+ */
+BCJR_API int bcjr_fb_backward(const float *seq, const float *cb, const float *T_dev,
+                     const float *soft, const float *grad_soft,
+                     int B, int N, int L, int k, int V,
+                     float *d_seq,
+                     void *ws, size_t ws_bytes, bcjr_stream_t stream);
+
+/*
+ * Full internals for return_internals=True (forward_backward.py:202-204,
+ * :230-231): P, log_alpha, log_beta, each (B, N, 2^L) fp32, natural log.
+ * Any of the three may be NULL.  O(B N 2^L) output: for diagnostics only
+ * (src/bcjr/anneal.py:143-184).
+ */
+BCJR_API int bcjr_fb_internals(const float *seq, const float *cb, const float *T_dev,
+                      int B, int N, int L, int k, int V,
+                      float *P, float *log_alpha, float *log_beta,
+                      void *ws, size_t ws_bytes, bcjr_stream_t stream);
+
+/* Device-side status of the last call that used `ws` (synchronises
+ * `stream`): BCJR_OK, or BCJR_ERR_TIMEOUT if a bounded wait gave up. */
+BCJR_API int bcjr_ws_status(const void *ws, bcjr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BCJR_B200_H */

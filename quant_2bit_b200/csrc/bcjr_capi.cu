@@ -1,0 +1,206 @@
+// C ABI of libbcjr_b200 (declared in include/bcjr_b200.h).
+//
+// Validates shapes and pointers, sizes the persistent grid from the caller's
+// workspace, and launches the kernels on the caller's stream.  No host
+// synchronisation, no allocation, T is read on the device.
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/bcjr_b200.h"
+#include "bcjr_kernels.h"
+
+namespace {
+
+constexpr size_t kHeaderBytes = 256;  // status word + padding (keeps data 256-B aligned)
+
+struct DevInfo {
+    int sms = 0;
+    int major = 0;
+    bool ok = false;
+};
+
+int query_device(DevInfo &d) {
+    static std::mutex mu;
+    static DevInfo cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BCJR_ERR_DEVICE;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!cache[dev].ok) {
+        int sms = 0, major = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+            return BCJR_ERR_DEVICE;
+        cache[dev].sms = sms;
+        cache[dev].major = major;
+        cache[dev].ok = true;
+    }
+    d = cache[dev];
+    if (d.major != 10) return BCJR_ERR_DEVICE;  // built for sm_100a only
+    return BCJR_OK;
+}
+
+bool built_combo(int b, int V) {
+    switch (b * 10 + V) {
+        case 11: case 21: case 31: case 41: case 22: case 42: return true;
+        default: return false;
+    }
+}
+
+int check_shape(int B, int N, int L, int k, int V) {
+    if (B < 0 || N < 1 || N > (1 << 20) || L < 1 || k < 1 || V < 1) return BCJR_ERR_BAD_SHAPE;
+    if (V > 2 || k > 4) return BCJR_ERR_UNSUPPORTED;
+    const int b = k * V;
+    if (b > 4 || !built_combo(b, V)) return BCJR_ERR_UNSUPPORTED;
+    if (L < b || L > 16) return BCJR_ERR_UNSUPPORTED;
+    if ((long long)B * N * V > (1LL << 40)) return BCJR_ERR_BAD_SHAPE;
+    return BCJR_OK;
+}
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+size_t data_bytes(int B, int N, int L, int b, int V, int mode, int sms) {
+    return bcjr::generic_workspace_bytes(B, N, L, b, V, mode, sms);
+}
+
+int prepare(bcjr::LaunchArgs &a, void *ws, size_t ws_bytes, int mode) {
+    DevInfo d;
+    int st = query_device(d);
+    if (st) return st;
+    if (!ws) return BCJR_ERR_WORKSPACE;
+    if (!aligned(ws, 256)) return BCJR_ERR_ALIGNMENT;
+    const size_t need = data_bytes(a.B, a.N, a.L, a.BB, a.V, mode, d.sms);
+    if (ws_bytes < kHeaderBytes + need) return BCJR_ERR_WORKSPACE;
+    a.status = reinterpret_cast<int *>(ws);
+    a.ws_data = static_cast<char *>(ws) + kHeaderBytes;
+    a.ws_data_bytes = ws_bytes - kHeaderBytes;
+    a.mode = mode;
+    a.grid = bcjr::generic_grid(a.B, a.N, a.L, a.BB, mode, a.ws_data_bytes);
+    if (a.grid < 1) return BCJR_ERR_WORKSPACE;
+    if (cudaMemsetAsync(a.status, 0, sizeof(int), a.stream) != cudaSuccess) return BCJR_ERR_LAUNCH;
+    return BCJR_OK;
+}
+
+int finish(cudaError_t e) {
+    return e == cudaSuccess ? BCJR_OK : BCJR_ERR_LAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bcjr_version(void) { return 100; }
+
+const char *bcjr_status_string(int status) {
+    switch (status) {
+        case BCJR_OK: return "ok";
+        case BCJR_ERR_BAD_SHAPE: return "bad shape (B, N, L, k, V inconsistent or out of range)";
+        case BCJR_ERR_UNSUPPORTED: return "unsupported trellis (need 1 <= kV <= 4, V <= 2, kV <= L <= 16)";
+        case BCJR_ERR_NULL_POINTER: return "a required pointer is NULL";
+        case BCJR_ERR_ALIGNMENT: return "pointer misaligned";
+        case BCJR_ERR_WORKSPACE: return "workspace missing or too small";
+        case BCJR_ERR_LAUNCH: return "CUDA launch failed";
+        case BCJR_ERR_DEVICE: return "no usable sm_100 device";
+        case BCJR_ERR_TIMEOUT: return "a bounded device-side wait gave up";
+        default: return "unknown status";
+    }
+}
+
+int bcjr_check_shape(int B, int N, int L, int k, int V) { return check_shape(B, N, L, k, V); }
+
+size_t bcjr_workspace_bytes(int B, int N, int L, int k, int V, int flags) {
+    if (check_shape(B, N, L, k, V)) return 0;
+    DevInfo d;
+    if (query_device(d)) return 0;
+    const int b = k * V;
+    size_t need = 0;
+    if (flags & BCJR_WS_FORWARD) {
+        size_t x = data_bytes(B, N, L, b, V, bcjr::kModeForward, d.sms);
+        if (x > need) need = x;
+    }
+    if (flags & BCJR_WS_BACKWARD) {
+        size_t x = data_bytes(B, N, L, b, V, bcjr::kModeBackward, d.sms);
+        if (x > need) need = x;
+    }
+    if (flags & BCJR_WS_INTERNALS) {
+        size_t x = data_bytes(B, N, L, b, V, bcjr::kModeInternals, d.sms);
+        if (x > need) need = x;
+    }
+    return kHeaderBytes + need;
+}
+
+int bcjr_fb_forward(const float *seq, const float *cb, const float *T_dev,
+                    int B, int N, int L, int k, int V,
+                    float *soft, float *logZ,
+                    void *ws, size_t ws_bytes, bcjr_stream_t stream) {
+    int st = check_shape(B, N, L, k, V);
+    if (st) return st;
+    if (B == 0) return BCJR_OK;
+    if (!seq || !cb || !T_dev || !soft) return BCJR_ERR_NULL_POINTER;
+    if (!aligned(seq, 4) || !aligned(cb, 4) || !aligned(T_dev, 4) || !aligned(soft, 4) ||
+        (logZ && !aligned(logZ, 4)))
+        return BCJR_ERR_ALIGNMENT;
+    bcjr::LaunchArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.seq = seq; a.cb = cb; a.T_dev = T_dev;
+    a.B = B; a.N = N; a.L = L; a.BB = k * V; a.V = V;
+    a.soft = soft; a.logZ = logZ;
+    a.stream = reinterpret_cast<cudaStream_t>(stream);
+    st = prepare(a, ws, ws_bytes, bcjr::kModeForward);
+    if (st) return st;
+    return finish(bcjr::launch_generic(a));
+}
+
+int bcjr_fb_backward(const float *seq, const float *cb, const float *T_dev,
+                     const float *soft, const float *grad_soft,
+                     int B, int N, int L, int k, int V,
+                     float *d_seq,
+                     void *ws, size_t ws_bytes, bcjr_stream_t stream) {
+    int st = check_shape(B, N, L, k, V);
+    if (st) return st;
+    if (B == 0) return BCJR_OK;
+    if (!seq || !cb || !T_dev || !soft || !grad_soft || !d_seq) return BCJR_ERR_NULL_POINTER;
+    if (!aligned(seq, 4) || !aligned(cb, 4) || !aligned(T_dev, 4) || !aligned(soft, 4) ||
+        !aligned(grad_soft, 4) || !aligned(d_seq, 4))
+        return BCJR_ERR_ALIGNMENT;
+    bcjr::LaunchArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.seq = seq; a.cb = cb; a.T_dev = T_dev;
+    a.soft_in = soft; a.grad = grad_soft;
+    a.B = B; a.N = N; a.L = L; a.BB = k * V; a.V = V;
+    a.dseq = d_seq;
+    a.stream = reinterpret_cast<cudaStream_t>(stream);
+    st = prepare(a, ws, ws_bytes, bcjr::kModeBackward);
+    if (st) return st;
+    return finish(bcjr::launch_generic(a));
+}
+
+int bcjr_fb_internals(const float *seq, const float *cb, const float *T_dev,
+                      int B, int N, int L, int k, int V,
+                      float *P, float *log_alpha, float *log_beta,
+                      void *ws, size_t ws_bytes, bcjr_stream_t stream) {
+    int st = check_shape(B, N, L, k, V);
+    if (st) return st;
+    if (B == 0) return BCJR_OK;
+    if (!seq || !cb || !T_dev) return BCJR_ERR_NULL_POINTER;
+    bcjr::LaunchArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.seq = seq; a.cb = cb; a.T_dev = T_dev;
+    a.B = B; a.N = N; a.L = L; a.BB = k * V; a.V = V;
+    a.P = P; a.LA = log_alpha; a.LB = log_beta;
+    a.stream = reinterpret_cast<cudaStream_t>(stream);
+    st = prepare(a, ws, ws_bytes, bcjr::kModeInternals);
+    if (st) return st;
+    return finish(bcjr::launch_generic(a));
+}
+
+int bcjr_ws_status(const void *ws, bcjr_stream_t stream) {
+    if (!ws) return BCJR_ERR_WORKSPACE;
+    int h = 0;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(&h, ws, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return BCJR_ERR_LAUNCH;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return BCJR_ERR_LAUNCH;
+    return h;
+}
+
+}  // extern "C"

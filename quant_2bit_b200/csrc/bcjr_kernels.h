@@ -1,0 +1,31 @@
+// Internal launch interface between the C ABI (bcjr_capi.cu) and the kernels.
+#pragma once
+
+#include <cstddef>
+#include <cuda_runtime.h>
+
+namespace bcjr {
+
+enum { kModeForward = 0, kModeBackward = 1, kModeInternals = 2 };
+
+struct LaunchArgs {
+    const float *seq, *cb, *T_dev;
+    const float *soft_in, *grad;  // backward inputs
+    int B, N, L, BB, V;
+    float *soft, *logZ;           // forward outputs
+    float *dseq;                  // backward output
+    float *P, *LA, *LB;           // internals outputs
+    void *ws_data;                // workspace after the header
+    size_t ws_data_bytes;
+    int *status;                  // device status word in the workspace header
+    int mode;
+    int grid;
+    cudaStream_t stream;
+};
+
+// Generic path (bcjr_generic.cu).
+size_t generic_workspace_bytes(int B, int N, int L, int BB, int V, int mode, int num_sms);
+int generic_grid(int B, int N, int L, int BB, int mode, size_t ws_data_bytes);
+cudaError_t launch_generic(const LaunchArgs &a);
+
+}  // namespace bcjr

@@ -1,0 +1,121 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Runs only where the reference checkout is importable (pass its root with
+--ref; it is not needed by the tests, which read the committed .npz files).
+Each fixture holds the inputs and the outputs of the reference's eager
+``bcjr_forward_backward`` (src/bcjr/forward_backward.py:190-232) with
+autograd backward, run on CPU in float32 (the parity target) and in float64
+(the same reference code with float64 tensors, for error attribution).
+
+Input generation follows the benchmark configs: torch.Generator seeded with
+``seed``; the codebook is drawn first, then the weights; Student-t weights use
+numpy.random.default_rng(seed).standard_t(3) / sqrt(3).
+
+    python tests/golden/make_golden.py --ref <reference root> [--only c1|small|l16|v2]
+"""
+import argparse
+import math
+import os
+import sys
+import time
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+T_SWEEP = (4.0, 2.0, 1.0, 0.5, 0.25, 0.1, 0.05)
+
+
+def run_ref(ref_fb, w, cb, T, L, k, V, grad):
+    out = {}
+    for tag, dt in (("32", torch.float32), ("64", torch.float64)):
+        x = torch.from_numpy(w).to(dt).clone().requires_grad_(True)
+        soft, lz = ref_fb(x, torch.from_numpy(cb).to(dt), float(T), L=L, k=k, V=V)
+        (soft * torch.from_numpy(grad).to(dt)).sum().backward()
+        out["soft" + tag] = soft.detach().numpy()
+        out["logZ" + tag] = lz.detach().numpy()
+        out["dseq" + tag] = x.grad.numpy()
+    return out
+
+
+def save(name, **arrs):
+    path = os.path.join(HERE, name)
+    np.savez_compressed(path, **arrs)
+    print("wrote", path, flush=True)
+
+
+def gen_c1(ref_fb):
+    # Config 1: L=8, k=2, V=1, N=256, 64 sequences, T=1, grad = ones.
+    L, k, V, N, B, T = 8, 2, 1, 256, 64, 1.0
+    g = torch.Generator().manual_seed(0)
+    cb = torch.randn(1 << L, V, generator=g).numpy()
+    w = torch.randn(B, N, V, generator=g).numpy()
+    for tag, grad in (("ones", np.ones_like(w)),
+                      ("randgrad", torch.randn(B, N, V, generator=torch.Generator().manual_seed(1)).numpy())):
+        out = run_ref(ref_fb, w, cb, T, L, k, V, grad)
+        save(f"c1_{tag}.npz", cb=cb, w=w, grad=grad, T=np.float64(T),
+             L=L, k=k, V=V, **out)
+
+
+def gen_small(ref_fb):
+    cases = [  # (L, k, V, N, B, T)
+        (4, 2, 1, 8, 3, 1.0), (6, 2, 1, 32, 4, 0.5), (6, 1, 1, 20, 3, 0.8),
+        (10, 2, 1, 64, 4, 0.5), (8, 2, 2, 32, 4, 1.0), (12, 2, 2, 16, 2, 0.5),
+        (9, 3, 1, 24, 3, 0.7), (12, 2, 1, 96, 2, 0.25),
+    ]
+    for (L, k, V, N, B, T) in cases:
+        g = torch.Generator().manual_seed(7 + L + 10 * V + 100 * k)
+        cb = torch.randn(1 << L, V, generator=g).numpy()
+        w = (1.3 * torch.randn(B, N, V, generator=g)).numpy()
+        grad = torch.randn(B, N, V, generator=g).numpy()
+        out = run_ref(ref_fb, w, cb, T, L, k, V, grad)
+        save(f"small_L{L}_k{k}_V{V}.npz", cb=cb, w=w, grad=grad, T=np.float64(T),
+             L=L, k=k, V=V, **out)
+
+
+def gen_l16(ref_fb, nseq=2):
+    # Config 2/4 inputs: codebook randn(65536,1), weights randn(4096,256,1)
+    # (first nseq sequences kept), T sweep; plus Student-t(3)/sqrt(3) weights.
+    L, k, V, N = 16, 2, 1, 256
+    g = torch.Generator().manual_seed(0)
+    cb = torch.randn(1 << L, V, generator=g).numpy()
+    w_all = torch.randn(4096, N, V, generator=g)
+    w_gauss = w_all[:nseq].numpy().copy()
+    w_t3 = (np.random.default_rng(0).standard_t(3, size=(nseq, N, V)) / math.sqrt(3.0)).astype(np.float32)
+    grad = torch.randn(nseq, N, V, generator=torch.Generator().manual_seed(1)).numpy()
+    np.save(os.path.join(HERE, "l16_cb.npy"), cb)
+    for dist, w in (("gauss", w_gauss), ("t3", w_t3)):
+        for T in T_SWEEP:
+            t0 = time.time()
+            out = run_ref(ref_fb, w, cb, T, L, k, V, grad)
+            save(f"l16_{dist}_T{T:g}.npz", w=w, grad=grad, T=np.float64(T),
+                 L=L, k=k, V=V, **out)
+            print(f"  {dist} T={T}: {time.time() - t0:.0f}s", flush=True)
+
+
+def gen_v2(ref_fb):
+    # The production drop-in shape: L=16, k=2, V=2 (16 predecessors), N=128.
+    L, k, V, N, B, T = 16, 2, 2, 128, 1, 0.5
+    g = torch.Generator().manual_seed(3)
+    cb = torch.randn(1 << L, V, generator=g).numpy()
+    w = torch.randn(B, N, V, generator=g).numpy()
+    grad = torch.randn(B, N, V, generator=g).numpy()
+    out = run_ref(ref_fb, w, cb, T, L, k, V, grad)
+    save("l16_v2.npz", cb=cb, w=w, grad=grad, T=np.float64(T), L=L, k=k, V=V, **out)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", required=True, help="root of the reference checkout")
+    ap.add_argument("--only", default=None)
+    args = ap.parse_args()
+    sys.path.insert(0, args.ref)
+    from src.bcjr.forward_backward import bcjr_forward_backward as ref_fb
+    torch.set_num_threads(os.cpu_count() or 1)
+    todo = [args.only] if args.only else ["small", "c1", "v2", "l16"]
+    for what in todo:
+        {"c1": gen_c1, "small": gen_small, "l16": gen_l16, "v2": gen_v2}[what](ref_fb)
+
+
+if __name__ == "__main__":
+    main()
