@@ -4,6 +4,7 @@
 // workspace, and launches the kernels on the caller's stream.  No host
 // synchronisation, no allocation, T is read on the device.
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -59,7 +60,18 @@ int check_shape(int B, int N, int L, int k, int V) {
 
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// The cluster kernel serves L=16, k=2, V=1 (forward and backward); every
+// other shape, the internals, and BCJR_B200_FORCE_GENERIC=1 take the generic
+// kernels.
+bool use_l16(int B, int N, int L, int b, int V, int mode) {
+    if (mode == bcjr::kModeInternals) return false;
+    const char *env = std::getenv("BCJR_B200_FORCE_GENERIC");
+    if (env && env[0] == '1') return false;
+    return bcjr::l16_applicable(B, N, L, b, V) && bcjr::l16_clusters(B, mode) > 0;
+}
+
 size_t data_bytes(int B, int N, int L, int b, int V, int mode, int sms) {
+    if (use_l16(B, N, L, b, V, mode)) return bcjr::l16_workspace_bytes(B, N, mode);
     return bcjr::generic_workspace_bytes(B, N, L, b, V, mode, sms);
 }
 
@@ -75,7 +87,8 @@ int prepare(bcjr::LaunchArgs &a, void *ws, size_t ws_bytes, int mode) {
     a.ws_data = static_cast<char *>(ws) + kHeaderBytes;
     a.ws_data_bytes = ws_bytes - kHeaderBytes;
     a.mode = mode;
-    a.grid = bcjr::generic_grid(a.B, a.N, a.L, a.BB, mode, a.ws_data_bytes);
+    a.fast = use_l16(a.B, a.N, a.L, a.BB, a.V, mode);
+    a.grid = a.fast ? 1 : bcjr::generic_grid(a.B, a.N, a.L, a.BB, mode, a.ws_data_bytes);
     if (a.grid < 1) return BCJR_ERR_WORKSPACE;
     if (cudaMemsetAsync(a.status, 0, sizeof(int), a.stream) != cudaSuccess) return BCJR_ERR_LAUNCH;
     return BCJR_OK;
@@ -83,6 +96,10 @@ int prepare(bcjr::LaunchArgs &a, void *ws, size_t ws_bytes, int mode) {
 
 int finish(cudaError_t e) {
     return e == cudaSuccess ? BCJR_OK : BCJR_ERR_LAUNCH;
+}
+
+cudaError_t launch(const bcjr::LaunchArgs &a) {
+    return a.fast ? bcjr::launch_l16(a) : bcjr::launch_generic(a);
 }
 
 }  // namespace
@@ -148,7 +165,7 @@ int bcjr_fb_forward(const float *seq, const float *cb, const float *T_dev,
     a.stream = reinterpret_cast<cudaStream_t>(stream);
     st = prepare(a, ws, ws_bytes, bcjr::kModeForward);
     if (st) return st;
-    return finish(bcjr::launch_generic(a));
+    return finish(launch(a));
 }
 
 int bcjr_fb_backward(const float *seq, const float *cb, const float *T_dev,
@@ -172,7 +189,7 @@ int bcjr_fb_backward(const float *seq, const float *cb, const float *T_dev,
     a.stream = reinterpret_cast<cudaStream_t>(stream);
     st = prepare(a, ws, ws_bytes, bcjr::kModeBackward);
     if (st) return st;
-    return finish(bcjr::launch_generic(a));
+    return finish(launch(a));
 }
 
 int bcjr_fb_internals(const float *seq, const float *cb, const float *T_dev,
@@ -191,7 +208,7 @@ int bcjr_fb_internals(const float *seq, const float *cb, const float *T_dev,
     a.stream = reinterpret_cast<cudaStream_t>(stream);
     st = prepare(a, ws, ws_bytes, bcjr::kModeInternals);
     if (st) return st;
-    return finish(bcjr::launch_generic(a));
+    return finish(launch(a));
 }
 
 int bcjr_ws_status(const void *ws, bcjr_stream_t stream) {

@@ -31,7 +31,10 @@
 //       Bb_{N-1}=0, Bb_t(r)    = sum_c sig_c [gam_{t+1}(s_c) + Bb_{t+1}(s_c mod 2^M)],
 //   where pi, sig are the softmax weights of the A and Bt LSEs, and
 //       dl_{t+1}(s_c) = P_{t+1}(s_c) (gam_{t+1}(s_c) + Bb_{t+1}(s_c mod 2^M) + H_{t+1}(r)),
-//       d_seq_u       = (2/T) sum_s dl_u(s) (c(s) - w_u).
+//       d_seq_u       = (2/T) sum_s dl_u(s) (c(s) - w_u)
+//                     = (2/T) sum_s dl_u(s) (c(s) - soft_u)     (sum_s dl_u(s) = 0).
+//   The second form is the one evaluated: it is exact in the mathematics and
+//   cancels any error common to all states (e.g. from rounding in soft_u).
 //   No atomics, no (B,N,S) buffers.
 #pragma once
 

@@ -220,9 +220,9 @@ gen_forward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                                  : nullptr;
             const float *Sc = sl.Ah + (long)tn * G;
             const float C = (float)(logZ2 - alpha_offset(sl.Off, tn) - U);
-            float acc[V];
+            double acc[V];  // per-thread partial in double: up to G/blockDim groups
 #pragma unroll
-            for (int v = 0; v < V; ++v) acc[v] = 0.f;
+            for (int v = 0; v < V; ++v) acc[v] = 0.0;
             float lmax = kNegInf;
             for (int r = threadIdx.x; r < G; r += blockDim.x) {
                 float x[NB];
@@ -246,12 +246,17 @@ gen_forward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 }
                 if (!internals) {
                     const float f = ex2(m + Sc[r] - C);
+                    float gsum[V];
+#pragma unroll
+                    for (int v = 0; v < V; ++v) gsum[v] = 0.f;
 #pragma unroll
                     for (int c = 0; c < NB; ++c) {
                         const long q = (long)r * NB + c;
 #pragma unroll
-                        for (int v = 0; v < V; ++v) acc[v] = fmaf(e[c] * f, __ldg(cb + q * V + v), acc[v]);
+                        for (int v = 0; v < V; ++v) gsum[v] = fmaf(e[c], __ldg(cb + q * V + v), gsum[v]);
                     }
+#pragma unroll
+                    for (int v = 0; v < V; ++v) acc[v] += (double)(f * gsum[v]);
                 }
             }
             smax.publish(lmax, t & 1);
@@ -260,10 +265,13 @@ gen_forward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 // record U (the shift of Rn's row) for row tn.
                 if (threadIdx.x == 0) sl.Uoff[tn] = U - (double)sigma;
             } else {
-                block_sum<V>(acc, sh);
+                float accf[V];
+#pragma unroll
+                for (int v = 0; v < V; ++v) accf[v] = (float)acc[v];
+                block_sum<V>(accf, sh);
                 if (threadIdx.x == 0) {
 #pragma unroll
-                    for (int v = 0; v < V; ++v) soft[((long)bs * N + tn) * V + v] = acc[v];
+                    for (int v = 0; v < V; ++v) soft[((long)bs * N + tn) * V + v] = accf[v];
                 }
             }
         }
@@ -326,12 +334,13 @@ gen_backward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             __syncthreads();
             const float sigma = (t == N - 2) ? 0.f : smax.read(tn & 1);
             U += (double)sigma;
-            float wt[V], gt[V];
+            float wt[V], gt[V], st[V];
             load_w<V>(w + (long)tn * V, wt);
             load_w<V>(g + (long)tn * V, gt);
+            load_w<V>(sf + (long)tn * V, st);
             float gs = 0.f;
 #pragma unroll
-            for (int v = 0; v < V; ++v) gs = fmaf(gt[v], __ldg(sf + (long)tn * V + v), gs);
+            for (int v = 0; v < V; ++v) gs = fmaf(gt[v], st[v], gs);
             const float *Rn = sl.Bt + (long)(tn & 1) * G;
             const float *Bbn = sl.Bb + (long)(tn & 1) * G;
             float *Ro = sl.Bt + (long)(t & 1) * G;
@@ -339,9 +348,13 @@ gen_backward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             const float *Sc = sl.Ah + (long)tn * G;
             const float *Hc = sl.Hh + (long)tn * G;
             const float C = (float)(logZ2 - alpha_offset(sl.Off, tn) - U);
-            float acc[V + 1];  // [0..V-1]: sum dl * c ; [V]: sum dl
+            // d_seq_u = (2/T) sum_s dl_u(s) (c(s) - soft_u): the reference's
+            // (2/T)(sum dl c - w sum dl) with sum_s dl_u(s) = 0 used exactly, which
+            // makes the result insensitive to a common shift of gam/H/Bb (e.g.
+            // the rounding of soft_u used to centre gam).
+            double acc[V];  // per-thread partial in double: up to G/blockDim groups
 #pragma unroll
-            for (int v = 0; v <= V; ++v) acc[v] = 0.f;
+            for (int v = 0; v < V; ++v) acc[v] = 0.0;
             float lmax = kNegInf;
             for (int r = threadIdx.x; r < G; r += blockDim.x) {
                 float x[NB], y[NB];
@@ -372,21 +385,27 @@ gen_backward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 }
                 const float f = ex2(m + Sc[r] - C);
                 const float hr = Hc[r];
+                float gsum[V];
+#pragma unroll
+                for (int v = 0; v < V; ++v) gsum[v] = 0.f;
 #pragma unroll
                 for (int c = 0; c < NB; ++c) {
                     const long q = (long)r * NB + c;
-                    const float dl = e[c] * f * (y[c] + hr);
-                    acc[V] += dl;
+                    const float dl = e[c] * (y[c] + hr);
 #pragma unroll
-                    for (int v = 0; v < V; ++v) acc[v] = fmaf(dl, __ldg(cb + q * V + v), acc[v]);
+                    for (int v = 0; v < V; ++v) gsum[v] = fmaf(dl, __ldg(cb + q * V + v) - st[v], gsum[v]);
                 }
+#pragma unroll
+                for (int v = 0; v < V; ++v) acc[v] += (double)(f * gsum[v]);
             }
             smax.publish(lmax, t & 1);
-            block_sum<V + 1>(acc, sh);
+            float accf[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v) accf[v] = (float)acc[v];
+            block_sum<V>(accf, sh);
             if (threadIdx.x == 0) {
 #pragma unroll
-                for (int v = 0; v < V; ++v)
-                    dseq[((long)bs * N + tn) * V + v] = two_over_T * (acc[v] - wt[v] * acc[V]);
+                for (int v = 0; v < V; ++v) dseq[((long)bs * N + tn) * V + v] = two_over_T * accf[v];
             }
         }
         __syncthreads();

@@ -20,6 +20,7 @@ struct LaunchArgs {
     int *status;                  // device status word in the workspace header
     int mode;
     int grid;
+    bool fast;                    // cluster kernel (bcjr_l16.cu)
     cudaStream_t stream;
 };
 
@@ -27,5 +28,11 @@ struct LaunchArgs {
 size_t generic_workspace_bytes(int B, int N, int L, int BB, int V, int mode, int num_sms);
 int generic_grid(int B, int N, int L, int BB, int mode, size_t ws_data_bytes);
 cudaError_t launch_generic(const LaunchArgs &a);
+
+// Cluster path for L=16, k=2, V=1, 2 <= N <= 512 (bcjr_l16.cu).
+bool l16_applicable(int B, int N, int L, int BB, int V);
+int l16_clusters(int B, int mode);
+size_t l16_workspace_bytes(int B, int N, int mode);
+cudaError_t launch_l16(const LaunchArgs &a);
 
 }  // namespace bcjr
