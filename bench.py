@@ -181,6 +181,9 @@ def main():
     ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5"])
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sequences", type=int, default=0,
+                    help="use only this many sequences per GPU (small cases for ncu)")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -215,6 +218,9 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
     cb_cpu, w_cpu, total_seqs = make_inputs(args.config, rank, world)
+    if args.sequences:
+        w_cpu = w_cpu[:args.sequences].contiguous()
+        total_seqs = w_cpu.shape[0] * world
     cb = cb_cpu.to(dev)
     w = w_cpu.to(dev)
     Bl = w.shape[0]
@@ -284,7 +290,7 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t_max_ms = float(t.item())
-    edges_total = Bl * world * EDGES_PER_SEQ if args.config == "c2" else total_seqs * EDGES_PER_SEQ
+    edges_total = (Bl * world if args.config == "c2" or args.sequences else total_seqs) * EDGES_PER_SEQ
     value = edges_total * args.steps / (t_max_ms / 1e3)
 
     # e2e: the public autograd API with host buffers, H2D and D2H in the timed region.
@@ -301,23 +307,25 @@ def main():
         soft_host.copy_(s.detach(), non_blocking=True)
         dseq_host.copy_(x.grad, non_blocking=True)
 
-    for _ in range(max(1, args.warmup // 2)):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        dist.barrier()
-    e2e_value = edges_total * args.steps / (float(te.item()) / 1e3)
+    e2e_value = None
+    if not args.no_e2e:
+        for _ in range(max(1, args.warmup // 2)):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+            dist.barrier()
+        e2e_value = edges_total * args.steps / (float(te.item()) / 1e3)
 
     # roofline of the dominant kernel (MUFU-bound; algorithmic ops per launch)
     fwd_avg = sum(fwd_ms) / len(fwd_ms)
@@ -344,7 +352,7 @@ def main():
                                     "c3": "config 3: Llama-3.2-1B layer, sharded",
                                     "c5": "config 5: OLMoE MoE layer, sharded"}[args.config]
                        + " (L=16, k=2, V=1, N=256, T=0.5, fwd+bwd, grad=ones)",
-                       "sequences_per_gpu": Bl, "sequences_total": total_seqs if args.config != "c2" else Bl * world,
+                       "sequences_per_gpu": Bl, "sequences_total": Bl * world if (args.config == "c2" or args.sequences) else total_seqs,
                        "l2": "flushed between timed steps (256 MB write, outside the events)",
                        "collective": "NCCL all_gather of soft per step" if world > 1 else "none"},
             "clocks": clk,

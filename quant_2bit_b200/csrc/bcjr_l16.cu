@@ -6,37 +6,48 @@
 // With M = 14, the 2^16 states split into 4096 "butterflies"
 //     j in [0, 4096):  states q = p * 2^14 + 4 j + c,   p, c in 0..3.
 // In the forward (alpha) direction butterfly j reads the four group values
-// A_t(p 2^12 + j) (one per p) and writes A_{t+1}(4 j + c) (one per c); in the
-// backward (beta) direction it reads Bt_{t+1}(4 j + c) and writes
-// Bt_t(p 2^12 + j).  Every step touches the same 16 states per butterfly, so
-// each thread owns two butterflies for the whole kernel and keeps their 32
-// codebook values in registers: no codebook traffic at all after the first
-// load.  CTA r of the cluster owns butterflies [1024 r, 1024 r + 1024).
+// A_t(p 2^12 + j) and writes A_{t+1}(4 j + c); in the backward (beta)
+// direction it reads Bt_{t+1}(4 j + c) and writes Bt_t(p 2^12 + j).  Every
+// step touches the same 16 states per butterfly, so each thread owns two
+// butterflies for the whole kernel and keeps their 32 codebook values in
+// registers: no codebook traffic after the first load.  CTA r of the cluster
+// owns butterflies [1024 r, 1024 r + 1024).
+//
+// Arithmetic
+// ----------
+// Messages are costs in squared-distance units, a = -A / kappa and
+// b = -Bt / kappa (kappa = log2(e)/T), so that the energy-plus-message of a
+// state is one fma of the exact difference d = c - w:  x = d*d + a.  The
+// soft-min of four costs is  m - lg2(sum 2^(kappa (m - x))) / kappa,
+// m = min x, with every exponent one fma  kappa m - kappa x.  All FMA-pipe
+// work is issued as f32x2 pairs (add/sub/mul/fma.rn.f32x2): pairs over p in
+// the alpha direction, pairs of output groups in the beta direction, from
+// one register layout cq[jj][c][p/2].
 //
 // Exchange between steps
 // ----------------------
 // The outputs of a step are the inputs of butterflies spread over the whole
 // cluster (a perfect shuffle).  Producers push them straight into the
 // consumer CTA's shared memory with st.async ... mbarrier::complete_tx, into
-// a 3-deep ring of input buffers; each buffer has an mbarrier that the
-// consumer arms with the expected byte count.  The ring depth plus one
-// __syncthreads per step guarantee a buffer is never overwritten before
-// every thread of its CTA has read it (a producer writing buffer u+1 during
-// consumption u proves all CTAs finished consumption u-2).  Every wait is
-// bounded (about 1 s); on timeout the kernel records BCJR_ERR_TIMEOUT in the
-// workspace status word, stops waiting and sending, and runs to completion.
+// a double-buffered ring; the consumer arms each buffer's mbarrier with the
+// expected byte count.  Every step reads all its inputs first, then passes
+// one __syncthreads, then computes and sends; a producer that has received
+// the complete input of consumption u therefore knows that every CTA has
+// finished reading consumption u-1, whose buffer it is about to overwrite.
+// Each CTA's minimum output cost travels with the data (sent by warp 0 after
+// the next barrier), so every consumer renormalises by the exact global
+// minimum of the previous step; shifts accumulate in double.
 //
-// Renormalisation: each CTA's maximum output travels with the data (one
-// st.async per destination), so every consumer subtracts the exact global
-// maximum of the previous step; shifts accumulate in double.
+// Two sequences ("slots") are interleaved step by step so that one slot's
+// exchange latency hides behind the other's arithmetic.  Alpha / H rows go
+// to a global history with float4 stores; the backward-time sweep fetches
+// the rows it needs one step ahead with TMA bulk copies (cp.async.bulk) into
+// shared memory.  Per-step partial sums of soft / d_seq are written per CTA
+// and added in a fixed order by CTA 0: results are deterministic.
 //
-// Two sequences are interleaved step by step ("slots") so that one slot's
-// exchange latency hides behind the other's arithmetic.  Alpha/H rows go to
-// a global history (float4 stores, read back with L1-bypassing loads in the
-// backward-time sweep).  Per-step partial sums of soft / d_seq are written
-// per CTA and added in a fixed order by CTA 0: results are deterministic.
-//
-// The recursions are documented in bcjr_common.cuh.
+// Every wait is bounded (about 1 s); on timeout the kernel records
+// BCJR_ERR_TIMEOUT in the workspace status word, stops waiting and sending,
+// and runs to completion.  The recursions are documented in bcjr_common.cuh.
 #include <cstdint>
 
 #include "bcjr_common.cuh"
@@ -55,20 +66,24 @@ constexpr int kNT = 512;              // threads per CTA
 constexpr int kJPT = kJPC / kNT;      // 2 butterflies per thread
 constexpr int kSlots = 2;             // sequences in flight per cluster
 constexpr int kNMax = 512;            // longest sequence staged in shared memory
-constexpr int kRing = 3;              // input ring depth
 constexpr int kWarps = kNT / 32;
+constexpr float kPosInf = __builtin_huge_valf();
 
 template <bool GRAD>
-struct alignas(16) Smem {
-    float buf[kSlots][kRing][GRAD ? 2 : 1][kNJ];  // 16 KB per plane
-    float maxslot[kSlots][kRing][kCL];
+struct alignas(128) Smem {
+    static constexpr int kPlanes = GRAD ? 2 : 1;
+    float buf[kSlots][2][kPlanes][kNJ];   // input ring (16 KB per plane)
+    float hst[kSlots][kPlanes][kNJ];      // history rows staged by TMA: [p * 1024 + jl]
+    double offs[kSlots][kNMax];           // alpha shifts O_t
+    float maxslot[kSlots][2][kCL];        // per-CTA minimum cost riding with the data
     float w[kSlots][kNMax];
     float g[kSlots][GRAD ? kNMax : 4];
     float sf[kSlots][GRAD ? kNMax : 4];
-    float wmax[kSlots][kWarps];
+    float wmin[kSlots][kWarps];
     float wacc[kSlots][kWarps];
     float lz[kSlots][kCL][2];
-    unsigned long long full[kSlots][kRing];
+    unsigned long long full[kSlots][2];
+    unsigned long long hbar[kSlots];
 };
 
 // ---------------------------------------------------------------------------
@@ -130,6 +145,14 @@ __device__ __forceinline__ void st_async1(uint32_t addr, float a, uint32_t bar) 
 __device__ __forceinline__ void st_cluster(uint32_t addr, float a) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(a) : "memory");
 }
+// One TMA bulk copy global -> own shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
+                                         uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -138,8 +161,8 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // Bounded wait: ~1 s, then BCJR_ERR_TIMEOUT in the status word.  Once any
 // thread of the grid has failed, every later wait returns at once.
-__device__ __forceinline__ void wait_full(uint32_t bar, uint32_t parity, int *status,
-                                          bool &failed) {
+__device__ __forceinline__ void wait_bar(uint32_t bar, uint32_t parity, int *status,
+                                         bool &failed) {
     if (failed) return;
     if (mbar_try(bar, parity)) return;
     const unsigned long long t0 = global_ns();
@@ -159,27 +182,58 @@ __device__ __forceinline__ void wait_full(uint32_t bar, uint32_t parity, int *st
     }
 }
 
-__device__ __forceinline__ float max4(float a, float b, float c, float d) {
-    return fmaxf(fmaxf(a, b), fmaxf(c, d));
+// f32x2 pairs.
+struct F2 {
+    float x, y;
+};
+__device__ __forceinline__ F2 mk(float a, float b) { return F2{a, b}; }
+__device__ __forceinline__ F2 bc(float a) { return F2{a, a}; }
+#define BCJR_F2_BINOP(NAME, OP)                                                          \
+    __device__ __forceinline__ F2 NAME(F2 a, F2 b) {                                     \
+        F2 r;                                                                            \
+        asm("{ .reg .b64 A, B, D; mov.b64 A, {%2, %3}; mov.b64 B, {%4, %5};"             \
+            " " OP " D, A, B; mov.b64 {%0, %1}, D; }"                                    \
+            : "=f"(r.x), "=f"(r.y)                                                       \
+            : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));                                   \
+        return r;                                                                        \
+    }
+BCJR_F2_BINOP(add2, "add.rn.f32x2")
+BCJR_F2_BINOP(sub2, "sub.rn.f32x2")
+BCJR_F2_BINOP(mul2, "mul.rn.f32x2")
+#undef BCJR_F2_BINOP
+__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
+    F2 r;
+    asm("{ .reg .b64 A, B, C, D; mov.b64 A, {%2, %3}; mov.b64 B, {%4, %5};"
+        " mov.b64 C, {%6, %7}; fma.rn.f32x2 D, A, B, C; mov.b64 {%0, %1}, D; }"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return r;
 }
+__device__ __forceinline__ float min3(float a, float b, float c) {
+    float r;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float min4(float a, float b, float c, float d) {
+    return fminf(min3(a, b, c), d);
+}
+__device__ __forceinline__ F2 ex2p(F2 a) { return F2{ex2(a.x), ex2(a.y)}; }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
+// Soft-min accumulator (m, s): value = m - lg2 s, s = sum 2^(m - x).
+__device__ __forceinline__ void smin_merge(float &m, float &s, float m2, float s2) {
+    if (m2 < m) {
+        s = s * ex2(m2 - m) + s2;
+        m = m2;
+    } else if (m2 < kPosInf) {
+        s = s + s2 * ex2(m - m2);
+    }
 }
 
 // Workspace of one (cluster, slot): float offsets.
 struct SlotLayout {
-    long hist;      // A rows: N x kG  (row t holds S_t, t >= 1)
+    long hist;      // alpha cost rows: N x kG  (row t holds S_t, t >= 1)
     long hhist;     // H rows: N x kG  (backward only)
     long part;      // N x kCL per-step per-CTA partial sums
-    long off;       // kCL x N doubles (alpha shifts O_t, one copy per CTA)
     long total;
 };
 
@@ -189,8 +243,6 @@ __host__ __device__ inline SlotLayout slot_layout(int N, bool grad) {
     s.hist = p; p += (long)N * kG;
     s.hhist = p; if (grad) p += (long)N * kG;
     s.part = p; p += (long)N * kCL;
-    p = (p + 3) & ~3L;
-    s.off = p; p += 2L * kCL * N;
     s.total = (p + 63) & ~63L;   // 256-byte aligned slots
     return s;
 }
@@ -202,10 +254,12 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
            const float *__restrict__ grad, int B, int N,
            float *__restrict__ out, float *__restrict__ logZ_out,
            float *__restrict__ ws, int *status) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    Smem<GRAD> &sm = *reinterpret_cast<Smem<GRAD> *>(smem_raw);
-    constexpr int kPlanes = GRAD ? 2 : 1;
-    constexpr uint32_t kBytes = kPlanes * kNJ * 4 + kCL * 4;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    using SM = Smem<GRAD>;
+    SM &sm = *reinterpret_cast<SM *>(smem_raw);
+    constexpr int kPlanes = SM::kPlanes;
+    constexpr uint32_t kBytes = kPlanes * kNJ * 4 + kCL * 4;   // per consumption
+    constexpr uint32_t kRowBytes = kJPC * 4;                    // one TMA chunk
 
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -215,19 +269,28 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     const SlotLayout lay = slot_layout(N, GRAD);
 
     const float T = __ldg(T_dev);
-    const float nk = -kLog2e / T;        // -kappa
+    const float kap = kLog2e / T;           // kappa
+    const float ikap = T / kLog2e;
     const float two_over_T = 2.f / T;
+    const float a0 = -(float)kB * ikap;     // cost of A_0 = b everywhere
 
-    // Codebook of my two butterflies: cbr[jj][p][c] = c(p 2^14 + 4 j + c).
+    // Codebook of my two butterflies:
+    // cq[jj][c][h] = (c(2h, c), c(2h+1, c)),  c(p, c) = cb[p 2^14 + 4 j + c].
     int jg[kJPT];
-    float cbr[kJPT][4][4];
+    F2 cq[kJPT][4][2];
 #pragma unroll
     for (int jj = 0; jj < kJPT; ++jj) {
         jg[jj] = (int)rank * kJPC + tid + kNT * jj;
+        float v[4][4];
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(cb + p * kG + 4 * jg[jj]));
-            cbr[jj][p][0] = v.x; cbr[jj][p][1] = v.y; cbr[jj][p][2] = v.z; cbr[jj][p][3] = v.w;
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(cb + p * kG + 4 * jg[jj]));
+            v[p][0] = q.x; v[p][1] = q.y; v[p][2] = q.z; v[p][3] = q.w;
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            cq[jj][c][0] = mk(v[0][c], v[1][c]);
+            cq[jj][c][1] = mk(v[2][c], v[3][c]);
         }
     }
 
@@ -240,14 +303,42 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     };
 
     if (tid == 0) {
-        for (int z = 0; z < kSlots; ++z)
-            for (int x = 0; x < kRing; ++x) mbar_init(sbase + soff(&sm.full[z][x]), 1);
+        for (int z = 0; z < kSlots; ++z) {
+            for (int x = 0; x < 2; ++x) mbar_init(sbase + soff(&sm.full[z][x]), 1);
+            mbar_init(sbase + soff(&sm.hbar[z]), 1);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     cluster_sync();
 
     bool failed = false;
-    uint32_t use[kSlots] = {0, 0};   // consumptions per slot (ring position, parity)
+    uint32_t use[kSlots] = {0, 0};    // ring consumptions per slot
+    uint32_t hcnt[kSlots] = {0, 0};   // TMA row loads waited per slot
+
+    // Deferred per-step tail (warp 0, after the next barrier): send the CTA's
+    // minimum output cost of step (pz) to the four consumers' ring slot pnb,
+    // and/or write the CTA partial sum of step pt.
+    int pz = -1, pnb = 0, pt = 0;
+    bool psend = false, ppart = false;
+    auto run_tail = [&](float *const *slot_ws) {
+        if (warp == 0 && pz >= 0) {
+            if (psend) {
+                float v = lane < kWarps ? sm.wmin[pz][lane] : kPosInf;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+                if (lane < kCL && !failed)
+                    st_async1(cbase[lane] + soff(&sm.maxslot[pz][pnb][rank]), v,
+                              cbase[lane] + soff(&sm.full[pz][pnb]));
+            }
+            if (ppart) {
+                float a = lane < kWarps ? sm.wacc[pz][lane] : 0.f;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                if (lane == 0) slot_ws[pz][lay.part + (long)pt * kCL + rank] = a;
+            }
+        }
+        pz = -1;
+    };
 
     for (long pair = cid; pair * kSlots < B; pair += ncl) {
         bool active[kSlots];
@@ -272,32 +363,33 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             }
         }
         __syncthreads();
+        // With one active slot the tail of a step must go out before that
+        // slot's next wait, so it runs at once behind an extra barrier.
+        const bool one_slot = !(active[0] && active[1]);
 
         // ------------------------------------------------------------ alpha
         double O[kSlots] = {0.0, 0.0};
-        float lzm[kSlots] = {kNegInf, kNegInf}, lzs[kSlots] = {0.f, 0.f};
+        float lzm[kSlots] = {kPosInf, kPosInf}, lzs[kSlots] = {0.f, 0.f};
         for (int t = 0; t < N; ++t) {
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
-                float *hist = slot_ws[z] + lay.hist;
-                float *hhist = slot_ws[z] + lay.hhist;
-                double *offs = reinterpret_cast<double *>(slot_ws[z] + lay.off) + (long)rank * N;
+                // (a) inputs: costs of A_t minus the global minimum, and H_t
                 float shift;
                 float ain[kJPT][4], hin[kJPT][4];
                 if (t == 0) {
-                    shift = (float)kB;            // S_0 = A_0 = b
+                    shift = a0;                    // a_0 is the same for every group
 #pragma unroll
                     for (int jj = 0; jj < kJPT; ++jj)
 #pragma unroll
                         for (int p = 0; p < 4; ++p) { ain[jj][p] = 0.f; hin[jj][p] = 0.f; }
                 } else {
-                    const int x = use[z] % kRing;
+                    const int x = use[z] & 1;
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
-                    wait_full(bar, (use[z] / kRing) & 1, status, failed);
+                    wait_bar(bar, (use[z] >> 1) & 1, status, failed);
                     const float4 mx = *reinterpret_cast<const float4 *>(sm.maxslot[z][x]);
-                    shift = max4(mx.x, mx.y, mx.z, mx.w);
+                    shift = min4(mx.x, mx.y, mx.z, mx.w);
 #pragma unroll
                     for (int jj = 0; jj < kJPT; ++jj) {
                         const int jl = tid + kNT * jj;
@@ -310,46 +402,51 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     ++use[z];
                 }
                 O[z] += (double)shift;
-                if (tid == 0) offs[t] = O[z];
-                const int nb = use[z] % kRing;       // ring slot of the next consumption
+                if (tid == 0) sm.offs[z][t] = O[z];
+                const int nb = use[z] & 1;
                 const float w = sm.w[z][t];
-                float gt = 0.f, gs = 0.f;
+                float gq = 0.f, gs = 0.f;
                 if (GRAD) {
-                    gt = sm.g[z][t];
-                    gs = gt * sm.sf[z][t];
+                    gq = sm.g[z][t];
+                    gs = gq * sm.sf[z][t];
                 }
+                // (b) everybody has read; (c) previous step's tail
+                __syncthreads();
+                run_tail(slot_ws);
+                // (d) compute and send
                 const bool last = (t == N - 1);
-                float lmax = kNegInf;
+                const F2 W = bc(w), Gq = bc(gq), GS = bc(-gs), NK = bc(-kap);
+                float lmin = kPosInf;
+                float *hist = slot_ws[z] + lay.hist;
+                float *hhist = slot_ws[z] + lay.hhist;
 #pragma unroll
                 for (int jj = 0; jj < kJPT; ++jj) {
+                    const F2 A01 = mk(ain[jj][0], ain[jj][1]), A23 = mk(ain[jj][2], ain[jj][3]);
+                    const F2 H01 = mk(hin[jj][0], hin[jj][1]), H23 = mk(hin[jj][2], hin[jj][3]);
                     float o4[4], h4[4];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        float xv[4];
-#pragma unroll
-                        for (int p = 0; p < 4; ++p) {
-                            const float d = cbr[jj][p][c] - w;
-                            xv[p] = fmaf(d, d * nk, ain[jj][p]);
-                        }
-                        const float m = max4(xv[0], xv[1], xv[2], xv[3]);
-                        float e[4], s = 0.f;
-#pragma unroll
-                        for (int p = 0; p < 4; ++p) { e[p] = ex2(xv[p] - m); s += e[p]; }
-                        o4[c] = m + lg2(s);
+                        const F2 d0 = sub2(cq[jj][c][0], W), d1 = sub2(cq[jj][c][1], W);
+                        const F2 x0 = fma2(d0, d0, A01), x1 = fma2(d1, d1, A23);
+                        const float m = min4(x0.x, x0.y, x1.x, x1.y);
+                        const F2 KM = bc(kap * m);
+                        const F2 e0 = ex2p(fma2(x0, NK, KM)), e1 = ex2p(fma2(x1, NK, KM));
+                        const F2 s2 = add2(e0, e1);
+                        const float s = s2.x + s2.y;
+                        o4[c] = fmaf(-lg2(s), ikap, m);
                         if (GRAD) {
-                            float hf = 0.f;
-#pragma unroll
-                            for (int p = 0; p < 4; ++p)
-                                hf = fmaf(e[p], fmaf(gt, cbr[jj][p][c], -gs) + hin[jj][p], hf);
-                            h4[c] = hf * rcp(s);
+                            const F2 f0 = add2(fma2(cq[jj][c][0], Gq, GS), H01);
+                            const F2 f1 = add2(fma2(cq[jj][c][1], Gq, GS), H23);
+                            const F2 hf = fma2(e0, f0, mul2(e1, f1));
+                            h4[c] = (hf.x + hf.y) * rcp(s);
                         }
                     }
-                    lmax = fmaxf(lmax, max4(o4[0], o4[1], o4[2], o4[3]));
+                    lmin = fminf(lmin, min4(o4[0], o4[1], o4[2], o4[3]));
                     const int j = jg[jj];
                     if (!last) {
                         const uint32_t dst = (uint32_t)(j >> 8) & 3u;
-                        const uint32_t o0 = soff(&sm.buf[z][nb][0][rank * kJPC + 4 * (j & 255)]);
                         const uint32_t bar = cbase[dst] + soff(&sm.full[z][nb]);
+                        const uint32_t o0 = soff(&sm.buf[z][nb][0][rank * kJPC + 4 * (j & 255)]);
                         if (!failed) {
                             st_async4(cbase[dst] + o0, o4[0], o4[1], o4[2], o4[3], bar);
                             if (GRAD) {
@@ -364,27 +461,26 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                                 make_float4(h4[0], h4[1], h4[2], h4[3]);
                     } else {
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) lse_merge(lzm[z], lzs[z], o4[c], 1.f);
+                        for (int c = 0; c < 4; ++c) smin_merge(lzm[z], lzs[z], kap * o4[c], 1.f);
                     }
                 }
                 if (!last) {
-                    lmax = warp_max(lmax);
-                    if (lane == 0) sm.wmax[z][warp] = lmax;
-                }
-                __syncthreads();
-                if (!last && tid == 0) {
-                    float cm = kNegInf;
-                    for (int i = 0; i < kWarps; ++i) cm = fmaxf(cm, sm.wmax[z][i]);
-                    const uint32_t om = soff(&sm.maxslot[z][nb][rank]);
-                    if (!failed)
 #pragma unroll
-                        for (int r = 0; r < kCL; ++r)
-                            st_async1(cbase[r] + om, cm, cbase[r] + soff(&sm.full[z][nb]));
+                    for (int o = 16; o > 0; o >>= 1) lmin = fminf(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
+                    if (lane == 0) sm.wmin[z][warp] = lmin;
+                }
+                pz = z; pnb = nb; psend = !last; ppart = false;
+                if (one_slot) {
+                    __syncthreads();
+                    run_tail(slot_ws);
                 }
             }
         }
+        __syncthreads();
+        run_tail(slot_ws);
+        __syncthreads();
 
-        // log2 Z = O_{N-1} + LSE over all 16384 values of S_N (four CTAs).
+        // log2 Z = -(kappa O_{N-1} + log2-soft-min over all 16384 costs kappa S_N).
 #pragma unroll
         for (int z = 0; z < kSlots; ++z) {
             if (!active[z]) continue;
@@ -393,17 +489,17 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             for (int o = 16; o > 0; o >>= 1) {
                 const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
                 const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-                lse_merge(m, s, m2, s2);
+                smin_merge(m, s, m2, s2);
             }
-            if (lane == 0) { sm.wmax[z][warp] = m; sm.wacc[z][warp] = s; }
+            if (lane == 0) { sm.wmin[z][warp] = m; sm.wacc[z][warp] = s; }
         }
         __syncthreads();
         if (tid == 0) {
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
-                float m = kNegInf, s = 0.f;
-                for (int i = 0; i < kWarps; ++i) lse_merge(m, s, sm.wmax[z][i], sm.wacc[z][i]);
+                float m = kPosInf, s = 0.f;
+                for (int i = 0; i < kWarps; ++i) smin_merge(m, s, sm.wmin[z][i], sm.wacc[z][i]);
 #pragma unroll
                 for (int r = 0; r < kCL; ++r) {
                     st_cluster(cbase[r] + soff(&sm.lz[z][rank][0]), m);
@@ -411,17 +507,41 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 }
             }
         }
-        cluster_sync();
+        cluster_sync();   // also publishes every CTA's history rows
+
         double logZ2[kSlots] = {0.0, 0.0};
 #pragma unroll
         for (int z = 0; z < kSlots; ++z) {
             if (!active[z]) continue;
-            float m = kNegInf, s = 0.f;
+            float m = kPosInf, s = 0.f;
 #pragma unroll
-            for (int r = 0; r < kCL; ++r) lse_merge(m, s, sm.lz[z][r][0], sm.lz[z][r][1]);
-            logZ2[z] = O[z] + (double)m + (double)log2f(s);
+            for (int r = 0; r < kCL; ++r) smin_merge(m, s, sm.lz[z][r][0], sm.lz[z][r][1]);
+            logZ2[z] = -((double)kap * O[z] + (double)m - (double)log2f(s));
             if (!GRAD && rank == 0 && tid == 0 && logZ_out)
                 logZ_out[sidx[z]] = (float)(logZ2[z] * (double)kLn2);
+        }
+
+        // Rows of step N-1 for the first beta step.
+        auto issue_rows = [&](int z, int tn) {
+            const uint32_t hb = sbase + soff(&sm.hbar[z]);
+            if (failed) return;
+            mbar_arm(hb, kPlanes * kNJ * 4);
+            const float *hist = slot_ws[z] + lay.hist + (long)tn * kG + rank * kJPC;
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+                bulk_g2s(sbase + soff(&sm.hst[z][0][p * kJPC]), hist + p * kNJ, kRowBytes, hb);
+            if (GRAD) {
+                const float *hh = slot_ws[z] + lay.hhist + (long)tn * kG + rank * kJPC;
+#pragma unroll
+                for (int p = 0; p < 4; ++p)
+                    bulk_g2s(sbase + soff(&sm.hst[z][kPlanes - 1][p * kJPC]), hh + p * kNJ, kRowBytes, hb);
+            }
+        };
+        if (tid == 0) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+#pragma unroll
+            for (int z = 0; z < kSlots; ++z)
+                if (active[z]) issue_rows(z, N - 1);
         }
 
         // ------------------------------------------------------------- beta
@@ -431,10 +551,8 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
-                const float *hist = slot_ws[z] + lay.hist;
-                const float *hhist = slot_ws[z] + lay.hhist;
-                const double *offs = reinterpret_cast<const double *>(slot_ws[z] + lay.off) + (long)rank * N;
-                float *part = slot_ws[z] + lay.part;
+                // (a) inputs: costs of Bt_{t+1} minus the global minimum, Bb_{t+1},
+                // and this step's alpha / H rows
                 float sigma;
                 float bin[kJPT][4], bbin[kJPT][4];
                 if (t == N - 2) {
@@ -444,12 +562,12 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
                         for (int c = 0; c < 4; ++c) { bin[jj][c] = 0.f; bbin[jj][c] = 0.f; }
                 } else {
-                    const int x = use[z] % kRing;
+                    const int x = use[z] & 1;
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
-                    wait_full(bar, (use[z] / kRing) & 1, status, failed);
+                    wait_bar(bar, (use[z] >> 1) & 1, status, failed);
                     const float4 mx = *reinterpret_cast<const float4 *>(sm.maxslot[z][x]);
-                    sigma = max4(mx.x, mx.y, mx.z, mx.w);
+                    sigma = min4(mx.x, mx.y, mx.z, mx.w);
 #pragma unroll
                     for (int jj = 0; jj < kJPT; ++jj) {
                         const int jl = tid + kNT * jj;
@@ -467,102 +585,130 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     ++use[z];
                 }
                 U[z] += (double)sigma;
-                const double Oa = tn > 0 ? offs[tn - 1] : 0.0;
-                const float C = (float)(logZ2[z] - Oa - U[z]);
-                const int nb = use[z] % kRing;
-                const float w = sm.w[z][tn];
-                float gt = 0.f, st = 0.f, gs = 0.f;
-                if (GRAD) {
-                    gt = sm.g[z][tn];
-                    st = sm.sf[z][tn];
-                    gs = gt * st;
+                float a4[kJPT][4], h4[kJPT][4];
+                if (tn > 0) {
+                    wait_bar(sbase + soff(&sm.hbar[z]), hcnt[z] & 1, status, failed);
+                    ++hcnt[z];
+#pragma unroll
+                    for (int jj = 0; jj < kJPT; ++jj) {
+                        const int jl = tid + kNT * jj;
+#pragma unroll
+                        for (int p = 0; p < 4; ++p) {
+                            a4[jj][p] = sm.hst[z][0][p * kJPC + jl];
+                            h4[jj][p] = GRAD ? sm.hst[z][kPlanes - 1][p * kJPC + jl] : 0.f;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < kJPT; ++jj)
+#pragma unroll
+                        for (int p = 0; p < 4; ++p) { a4[jj][p] = a0; h4[jj][p] = 0.f; }
                 }
-                float acc = 0.f, lmax = kNegInf;
+                const double Oa = tn > 0 ? sm.offs[z][tn - 1] : 0.0;
+                const float Cb = (float)(-(logZ2[z] + (double)kap * (Oa + U[z])));
+                const int nb = use[z] & 1;
+                const float w = sm.w[z][tn];
+                float gq = 0.f, gs = 0.f, st = 0.f;
+                if (GRAD) {
+                    gq = sm.g[z][tn];
+                    st = sm.sf[z][tn];
+                    gs = gq * st;
+                }
+                // (b) everybody has read ring and rows; (c) tail + next rows
+                __syncthreads();
+                run_tail(slot_ws);
+                if (tid == 0 && tn - 1 >= 1) issue_rows(z, tn - 1);
+                // (d) compute and send
+                const F2 W = bc(w), Gq = bc(gq), CB = bc(Cb), NK = bc(-kap), MIK = bc(-ikap),
+                         ST = bc(st);
+                F2 acc = bc(0.f);
+                float lmin = kPosInf;
 #pragma unroll
                 for (int jj = 0; jj < kJPT; ++jj) {
                     const int j = jg[jj];
-                    float a4[4], h4[4];
 #pragma unroll
-                    for (int p = 0; p < 4; ++p) {
-                        a4[p] = tn > 0 ? __ldcg(hist + (long)tn * kG + p * kNJ + j) : (float)kB;
-                        h4[p] = (GRAD && tn > 0) ? __ldcg(hhist + (long)tn * kG + p * kNJ + j) : 0.f;
-                    }
-#pragma unroll
-                    for (int p = 0; p < 4; ++p) {
-                        float xv[4], yv[4];
+                    for (int h = 0; h < 2; ++h) {          // output groups p' = 2h, 2h+1
+                        F2 xc[4];
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
-                            const float d = cbr[jj][p][c] - w;
-                            xv[c] = fmaf(d, d * nk, bin[jj][c]);
-                            if (GRAD) yv[c] = fmaf(gt, cbr[jj][p][c], -gs) + bbin[jj][c];
+                            const F2 d = sub2(cq[jj][c][h], W);
+                            xc[c] = fma2(d, d, bc(bin[jj][c]));
                         }
-                        const float m = max4(xv[0], xv[1], xv[2], xv[3]);
-                        float e[4], s = 0.f;
+                        const F2 M = mk(min4(xc[0].x, xc[1].x, xc[2].x, xc[3].x),
+                                        min4(xc[0].y, xc[1].y, xc[2].y, xc[3].y));
+                        const F2 KM = mk(kap * M.x, kap * M.y);
+                        F2 e[4];
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) { e[c] = ex2(xv[c] - m); s += e[c]; }
-                        const float f = ex2(m + a4[p] - C);
-                        float ob = 0.f, bbo = 0.f;
-                        if (t >= 0) ob = m + lg2(s);
+                        for (int c = 0; c < 4; ++c) e[c] = ex2p(fma2(xc[c], NK, KM));
+                        const F2 S = add2(add2(e[0], e[1]), add2(e[2], e[3]));
+                        const F2 f = ex2p(fma2(add2(M, mk(a4[jj][2 * h], a4[jj][2 * h + 1])), NK, CB));
+                        F2 ob = bc(0.f), bbo = bc(0.f);
+                        if (t >= 0) {
+                            ob = fma2(mk(lg2(S.x), lg2(S.y)), MIK, M);
+                            lmin = min3(lmin, ob.x, ob.y);
+                        }
                         if (!GRAD) {
-                            float ec = 0.f;
+                            F2 ec = mul2(e[0], cq[jj][0][h]);
 #pragma unroll
-                            for (int c = 0; c < 4; ++c) ec = fmaf(e[c], cbr[jj][p][c], ec);
-                            acc = fmaf(f, ec, acc);
+                            for (int c = 1; c < 4; ++c) ec = fma2(e[c], cq[jj][c][h], ec);
+                            acc = fma2(f, ec, acc);
                         } else {
-                            float ey = 0.f, dl = 0.f;
+                            const F2 Hh = mk(h4[jj][2 * h], h4[jj][2 * h + 1]);
+                            F2 ey = bc(0.f), dl = bc(0.f);
 #pragma unroll
                             for (int c = 0; c < 4; ++c) {
-                                ey = fmaf(e[c], yv[c], ey);
-                                dl = fmaf(e[c] * (yv[c] + h4[p]), cbr[jj][p][c] - st, dl);
+                                const F2 y = fma2(cq[jj][c][h], Gq, bc(bbin[jj][c] - gs));
+                                ey = fma2(e[c], y, ey);
+                                const F2 cm = sub2(cq[jj][c][h], ST);
+                                dl = fma2(mul2(e[c], add2(y, Hh)), cm, dl);
                             }
-                            bbo = ey * rcp(s);
-                            acc = fmaf(f, dl, acc);
+                            bbo = mul2(ey, mk(rcp(S.x), rcp(S.y)));
+                            acc = fma2(f, dl, acc);
                         }
-                        if (t >= 0) {
-                            lmax = fmaxf(lmax, ob);
-                            if (!failed) {
-                                const uint32_t bar = cbase[p] + soff(&sm.full[z][nb]);
-                                st_async1(cbase[p] + soff(&sm.buf[z][nb][0][j]), ob, bar);
-                                if (GRAD) st_async1(cbase[p] + soff(&sm.buf[z][nb][kPlanes - 1][j]), bbo, bar);
+                        if (t >= 0 && !failed) {
+                            const uint32_t ob0 = soff(&sm.buf[z][nb][0][j]);
+                            st_async1(cbase[2 * h] + ob0, ob.x, cbase[2 * h] + soff(&sm.full[z][nb]));
+                            st_async1(cbase[2 * h + 1] + ob0, ob.y, cbase[2 * h + 1] + soff(&sm.full[z][nb]));
+                            if (GRAD) {
+                                const uint32_t ob1 = soff(&sm.buf[z][nb][kPlanes - 1][j]);
+                                st_async1(cbase[2 * h] + ob1, bbo.x, cbase[2 * h] + soff(&sm.full[z][nb]));
+                                st_async1(cbase[2 * h + 1] + ob1, bbo.y, cbase[2 * h + 1] + soff(&sm.full[z][nb]));
                             }
                         }
                     }
                 }
-                acc = warp_sum(acc);
-                if (t >= 0) lmax = warp_max(lmax);
-                if (lane == 0) {
-                    sm.wacc[z][warp] = acc;
-                    sm.wmax[z][warp] = lmax;
-                }
-                __syncthreads();
-                if (tid == 0) {
-                    if (t >= 0) {
-                        float cm = kNegInf;
-                        for (int i = 0; i < kWarps; ++i) cm = fmaxf(cm, sm.wmax[z][i]);
-                        const uint32_t om = soff(&sm.maxslot[z][nb][rank]);
-                        if (!failed)
+                float a = acc.x + acc.y;
 #pragma unroll
-                            for (int r = 0; r < kCL; ++r)
-                                st_async1(cbase[r] + om, cm, cbase[r] + soff(&sm.full[z][nb]));
-                    }
-                    float sacc = 0.f;
-                    for (int i = 0; i < kWarps; ++i) sacc += sm.wacc[z][i];
-                    part[(long)tn * kCL + rank] = sacc;
+                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                if (t >= 0) {
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) lmin = fminf(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
+                }
+                if (lane == 0) {
+                    sm.wacc[z][warp] = a;
+                    sm.wmin[z][warp] = lmin;
+                }
+                pz = z; pnb = nb; psend = (t >= 0); ppart = true; pt = tn;
+                if (one_slot) {
+                    __syncthreads();
+                    run_tail(slot_ws);
                 }
             }
         }
+        __syncthreads();
+        run_tail(slot_ws);
 
         // Per-step partials of the four CTAs, added in a fixed order.
         cluster_sync();
         if (rank == 0) {
+            const float scale = GRAD ? two_over_T : 1.f;
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
                 const float *part = slot_ws[z] + lay.part;
                 for (int tn = tid; tn < N; tn += kNT) {
                     const float4 v = __ldcg(reinterpret_cast<const float4 *>(part + (long)tn * kCL));
-                    const float sum = ((v.x + v.y) + v.z) + v.w;
-                    out[sidx[z] * N + tn] = GRAD ? two_over_T * sum : sum;
+                    out[sidx[z] * N + tn] = scale * (((v.x + v.y) + v.z) + v.w);
                 }
             }
         }
