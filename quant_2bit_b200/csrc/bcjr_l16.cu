@@ -84,6 +84,8 @@ struct alignas(128) Smem {
     float lz[kSlots][kCL][2];
     unsigned long long full[kSlots][2];
     unsigned long long hbar[kSlots];
+    int mn[kSlots][2];                    // per-step CTA minimum (order-preserving int key)
+    int cnt[kSlots][2];                   // warps finished with the step
 };
 
 // ---------------------------------------------------------------------------
@@ -120,13 +122,14 @@ __device__ __forceinline__ void mbar_arm(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");
 }
+// try_wait suspends the thread until the phase completes or ~20 us pass.
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;"
+        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;"
         " selp.u32 %0, 1, 0, p; }"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(20000)
         : "memory");
     return ok != 0;
 }
@@ -168,7 +171,7 @@ __device__ __forceinline__ void wait_bar(uint32_t bar, uint32_t parity, int *sta
     const unsigned long long t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try(bar, parity)) return;
-        if ((i & 63) == 0) {
+        if ((i & 7) == 0) {
             if (*reinterpret_cast<volatile int *>(status) != 0) {
                 failed = true;
                 return;
@@ -182,33 +185,14 @@ __device__ __forceinline__ void wait_bar(uint32_t bar, uint32_t parity, int *sta
     }
 }
 
-// f32x2 pairs.
-struct F2 {
-    float x, y;
-};
-__device__ __forceinline__ F2 mk(float a, float b) { return F2{a, b}; }
-__device__ __forceinline__ F2 bc(float a) { return F2{a, a}; }
-#define BCJR_F2_BINOP(NAME, OP)                                                          \
-    __device__ __forceinline__ F2 NAME(F2 a, F2 b) {                                     \
-        F2 r;                                                                            \
-        asm("{ .reg .b64 A, B, D; mov.b64 A, {%2, %3}; mov.b64 B, {%4, %5};"             \
-            " " OP " D, A, B; mov.b64 {%0, %1}, D; }"                                    \
-            : "=f"(r.x), "=f"(r.y)                                                       \
-            : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));                                   \
-        return r;                                                                        \
-    }
-BCJR_F2_BINOP(add2, "add.rn.f32x2")
-BCJR_F2_BINOP(sub2, "sub.rn.f32x2")
-BCJR_F2_BINOP(mul2, "mul.rn.f32x2")
-#undef BCJR_F2_BINOP
-__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
-    F2 r;
-    asm("{ .reg .b64 A, B, C, D; mov.b64 A, {%2, %3}; mov.b64 B, {%4, %5};"
-        " mov.b64 C, {%6, %7}; fma.rn.f32x2 D, A, B, C; mov.b64 {%0, %1}, D; }"
-        : "=f"(r.x), "=f"(r.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return r;
-}
+// f32x2 pairs (FADD2 / FMUL2 / FFMA2 through the sm_100 float2 builtins).
+using F2 = float2;
+__device__ __forceinline__ F2 mk(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ F2 bc(float a) { return make_float2(a, a); }
+__device__ __forceinline__ F2 add2(F2 a, F2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ F2 sub2(F2 a, F2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }
+__device__ __forceinline__ F2 mul2(F2 a, F2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float min3(float a, float b, float c) {
     float r;
     asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -218,6 +202,15 @@ __device__ __forceinline__ float min4(float a, float b, float c, float d) {
     return fminf(min3(a, b, c), d);
 }
 __device__ __forceinline__ F2 ex2p(F2 a) { return F2{ex2(a.x), ex2(a.y)}; }
+
+// Order-preserving map float -> int (and back): a < b  <=>  key(a) < key(b).
+__device__ __forceinline__ int order_key(float f) {
+    const int i = __float_as_int(f);
+    return i >= 0 ? i : i ^ 0x7fffffff;
+}
+__device__ __forceinline__ float order_key_inv(int k) {
+    return __int_as_float(k >= 0 ? k : k ^ 0x7fffffff);
+}
 
 // Soft-min accumulator (m, s): value = m - lg2 s, s = sum 2^(m - x).
 __device__ __forceinline__ void smin_merge(float &m, float &s, float m2, float s2) {
@@ -233,7 +226,7 @@ __device__ __forceinline__ void smin_merge(float &m, float &s, float m2, float s
 struct SlotLayout {
     long hist;      // alpha cost rows: N x kG  (row t holds S_t, t >= 1)
     long hhist;     // H rows: N x kG  (backward only)
-    long part;      // N x kCL per-step per-CTA partial sums
+    long part;      // N x kCL x kWarps per-step per-warp partial sums
     long total;
 };
 
@@ -242,7 +235,7 @@ __host__ __device__ inline SlotLayout slot_layout(int N, bool grad) {
     long p = 0;
     s.hist = p; p += (long)N * kG;
     s.hhist = p; if (grad) p += (long)N * kG;
-    s.part = p; p += (long)N * kCL;
+    s.part = p; p += (long)N * kCL * kWarps;
     s.total = (p + 63) & ~63L;   // 256-byte aligned slots
     return s;
 }
@@ -302,7 +295,24 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         return (uint32_t)__cvta_generic_to_shared(p) - sbase;
     };
 
+    // Remote CTA of my alpha outputs and their offset inside an input plane.
+    uint32_t rdst[kJPT], aoff[kJPT];
+#pragma unroll
+    for (int jj = 0; jj < kJPT; ++jj) {
+        const int j = jg[jj];
+        rdst[jj] = cbase[0];
+        const uint32_t d = (uint32_t)(j >> 8) & 3u;
+#pragma unroll
+        for (int r = 1; r < kCL; ++r) rdst[jj] = (d == (uint32_t)r) ? cbase[r] : rdst[jj];
+        aoff[jj] = 4u * (rank * kJPC + 4 * (j & 255));
+    }
+
     if (tid == 0) {
+        for (int z = 0; z < kSlots; ++z)
+            for (int x = 0; x < 2; ++x) {
+                sm.mn[z][x] = order_key(kPosInf);
+                sm.cnt[z][x] = 0;
+            }
         for (int z = 0; z < kSlots; ++z) {
             for (int x = 0; x < 2; ++x) mbar_init(sbase + soff(&sm.full[z][x]), 1);
             mbar_init(sbase + soff(&sm.hbar[z]), 1);
@@ -312,32 +322,63 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     cluster_sync();
 
     bool failed = false;
-    uint32_t use[kSlots] = {0, 0};    // ring consumptions per slot
+    uint32_t use[kSlots] = {0, 0};    // ring consumptions per slot (uniform over the CTA)
     uint32_t hcnt[kSlots] = {0, 0};   // TMA row loads waited per slot
 
-    // Deferred per-step tail (warp 0, after the next barrier): send the CTA's
-    // minimum output cost of step (pz) to the four consumers' ring slot pnb,
-    // and/or write the CTA partial sum of step pt.
-    int pz = -1, pnb = 0, pt = 0;
-    bool psend = false, ppart = false;
-    auto run_tail = [&](float *const *slot_ws) {
-        if (warp == 0 && pz >= 0) {
-            if (psend) {
-                float v = lane < kWarps ? sm.wmin[pz][lane] : kPosInf;
+    // End of a step, per warp (no block barrier): the warp's minimum output
+    // cost goes into the step's shared-memory minimum, its partial sum into
+    // global memory, and the last warp to arrive sends the CTA minimum to the
+    // four consumers and, in the beta sweep, issues the next TMA rows (every
+    // warp of the CTA has read this step's inputs by then).
+    // TMA rows of step tn (alpha costs, and H for the backward) into the
+    // staging buffer of slot z; completion on hbar[z].
+    auto issue_rows = [&](int z, int tn, float *const *slot_ws) {
+        const uint32_t hb = sbase + soff(&sm.hbar[z]);
+        if (failed) return;
+        mbar_arm(hb, kPlanes * kNJ * 4);
+        const float *hist = slot_ws[z] + lay.hist + (long)tn * kG + rank * kJPC;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
-                if (lane < kCL && !failed)
-                    st_async1(cbase[lane] + soff(&sm.maxslot[pz][pnb][rank]), v,
-                              cbase[lane] + soff(&sm.full[pz][pnb]));
-            }
-            if (ppart) {
-                float a = lane < kWarps ? sm.wacc[pz][lane] : 0.f;
+        for (int p = 0; p < 4; ++p)
+            bulk_g2s(sbase + soff(&sm.hst[z][0][p * kJPC]), hist + p * kNJ, kRowBytes, hb);
+        if (GRAD) {
+            const float *hh = slot_ws[z] + lay.hhist + (long)tn * kG + rank * kJPC;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-                if (lane == 0) slot_ws[pz][lay.part + (long)pt * kCL + rank] = a;
+            for (int p = 0; p < 4; ++p)
+                bulk_g2s(sbase + soff(&sm.hst[z][kPlanes - 1][p * kJPC]), hh + p * kNJ, kRowBytes, hb);
+        }
+    };
+
+    auto finish_step = [&](int z, int nb, bool send, float lmin, float *part_row, float acc,
+                           int rows_tn, float *const *slot_ws) {
+        if (send) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) lmin = fminf(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
+        }
+        if (part_row) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        }
+        int last = 0;
+        if (lane == 0) {
+            if (part_row) part_row[warp] = acc;
+            if (send) atomicMin(&sm.mn[z][nb], order_key(lmin));
+            __threadfence_block();
+            last = atomicAdd(&sm.cnt[z][nb], 1) == kWarps - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence_block();
+            const int k = atomicOr(&sm.mn[z][nb], 0);
+            if (send && lane < kCL && !failed)
+                st_async1(cbase[lane] + soff(&sm.maxslot[z][nb][rank]), order_key_inv(k),
+                          cbase[lane] + soff(&sm.full[z][nb]));
+            if (rows_tn >= 1 && lane == 0) issue_rows(z, rows_tn, slot_ws);
+            __syncwarp();
+            if (lane == 0) {
+                sm.mn[z][nb] = order_key(kPosInf);
+                sm.cnt[z][nb] = 0;
             }
         }
-        pz = -1;
     };
 
     for (long pair = cid; pair * kSlots < B; pair += ncl) {
@@ -363,9 +404,6 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             }
         }
         __syncthreads();
-        // With one active slot the tail of a step must go out before that
-        // slot's next wait, so it runs at once behind an extra barrier.
-        const bool one_slot = !(active[0] && active[1]);
 
         // ------------------------------------------------------------ alpha
         double O[kSlots] = {0.0, 0.0};
@@ -374,7 +412,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
-                // (a) inputs: costs of A_t minus the global minimum, and H_t
+                // inputs: costs of A_t minus the global minimum, and H_t
                 float shift;
                 float ain[kJPT][4], hin[kJPT][4];
                 if (t == 0) {
@@ -410,15 +448,11 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     gq = sm.g[z][t];
                     gs = gq * sm.sf[z][t];
                 }
-                // (b) everybody has read; (c) previous step's tail
-                __syncthreads();
-                run_tail(slot_ws);
-                // (d) compute and send
                 const bool last = (t == N - 1);
                 const F2 W = bc(w), Gq = bc(gq), GS = bc(-gs), NK = bc(-kap);
                 float lmin = kPosInf;
-                float *hist = slot_ws[z] + lay.hist;
-                float *hhist = slot_ws[z] + lay.hhist;
+                float *hist = slot_ws[z] + lay.hist + (long)(t + 1) * kG;
+                float *hhist = slot_ws[z] + lay.hhist + (long)(t + 1) * kG;
 #pragma unroll
                 for (int jj = 0; jj < kJPT; ++jj) {
                     const F2 A01 = mk(ain[jj][0], ain[jj][1]), A23 = mk(ain[jj][2], ain[jj][3]);
@@ -444,40 +478,24 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     lmin = fminf(lmin, min4(o4[0], o4[1], o4[2], o4[3]));
                     const int j = jg[jj];
                     if (!last) {
-                        const uint32_t dst = (uint32_t)(j >> 8) & 3u;
-                        const uint32_t bar = cbase[dst] + soff(&sm.full[z][nb]);
-                        const uint32_t o0 = soff(&sm.buf[z][nb][0][rank * kJPC + 4 * (j & 255)]);
+                        const uint32_t bar = rdst[jj] + soff(&sm.full[z][nb]);
+                        const uint32_t o0 = rdst[jj] + soff(&sm.buf[z][nb][0][0]) + aoff[jj];
                         if (!failed) {
-                            st_async4(cbase[dst] + o0, o4[0], o4[1], o4[2], o4[3], bar);
-                            if (GRAD) {
-                                const uint32_t o1 = soff(&sm.buf[z][nb][kPlanes - 1][rank * kJPC + 4 * (j & 255)]);
-                                st_async4(cbase[dst] + o1, h4[0], h4[1], h4[2], h4[3], bar);
-                            }
+                            st_async4(o0, o4[0], o4[1], o4[2], o4[3], bar);
+                            if (GRAD)
+                                st_async4(o0 + kNJ * 4, h4[0], h4[1], h4[2], h4[3], bar);
                         }
-                        *reinterpret_cast<float4 *>(hist + (long)(t + 1) * kG + 4 * j) =
-                            make_float4(o4[0], o4[1], o4[2], o4[3]);
+                        *reinterpret_cast<float4 *>(hist + 4 * j) = make_float4(o4[0], o4[1], o4[2], o4[3]);
                         if (GRAD)
-                            *reinterpret_cast<float4 *>(hhist + (long)(t + 1) * kG + 4 * j) =
-                                make_float4(h4[0], h4[1], h4[2], h4[3]);
+                            *reinterpret_cast<float4 *>(hhist + 4 * j) = make_float4(h4[0], h4[1], h4[2], h4[3]);
                     } else {
 #pragma unroll
                         for (int c = 0; c < 4; ++c) smin_merge(lzm[z], lzs[z], kap * o4[c], 1.f);
                     }
                 }
-                if (!last) {
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) lmin = fminf(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
-                    if (lane == 0) sm.wmin[z][warp] = lmin;
-                }
-                pz = z; pnb = nb; psend = !last; ppart = false;
-                if (one_slot) {
-                    __syncthreads();
-                    run_tail(slot_ws);
-                }
+                finish_step(z, nb, !last, lmin, nullptr, 0.f, 0, slot_ws);
             }
         }
-        __syncthreads();
-        run_tail(slot_ws);
         __syncthreads();
 
         // log2 Z = -(kappa O_{N-1} + log2-soft-min over all 16384 costs kappa S_N).
@@ -520,28 +538,11 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             if (!GRAD && rank == 0 && tid == 0 && logZ_out)
                 logZ_out[sidx[z]] = (float)(logZ2[z] * (double)kLn2);
         }
-
-        // Rows of step N-1 for the first beta step.
-        auto issue_rows = [&](int z, int tn) {
-            const uint32_t hb = sbase + soff(&sm.hbar[z]);
-            if (failed) return;
-            mbar_arm(hb, kPlanes * kNJ * 4);
-            const float *hist = slot_ws[z] + lay.hist + (long)tn * kG + rank * kJPC;
-#pragma unroll
-            for (int p = 0; p < 4; ++p)
-                bulk_g2s(sbase + soff(&sm.hst[z][0][p * kJPC]), hist + p * kNJ, kRowBytes, hb);
-            if (GRAD) {
-                const float *hh = slot_ws[z] + lay.hhist + (long)tn * kG + rank * kJPC;
-#pragma unroll
-                for (int p = 0; p < 4; ++p)
-                    bulk_g2s(sbase + soff(&sm.hst[z][kPlanes - 1][p * kJPC]), hh + p * kNJ, kRowBytes, hb);
-            }
-        };
         if (tid == 0) {
             asm volatile("fence.proxy.async.global;" ::: "memory");
 #pragma unroll
             for (int z = 0; z < kSlots; ++z)
-                if (active[z]) issue_rows(z, N - 1);
+                if (active[z]) issue_rows(z, N - 1, slot_ws);
         }
 
         // ------------------------------------------------------------- beta
@@ -551,7 +552,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
-                // (a) inputs: costs of Bt_{t+1} minus the global minimum, Bb_{t+1},
+                // inputs: costs of Bt_{t+1} minus the global minimum, Bb_{t+1},
                 // and this step's alpha / H rows
                 float sigma;
                 float bin[kJPT][4], bbin[kJPT][4];
@@ -614,11 +615,6 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     st = sm.sf[z][tn];
                     gs = gq * st;
                 }
-                // (b) everybody has read ring and rows; (c) tail + next rows
-                __syncthreads();
-                run_tail(slot_ws);
-                if (tid == 0 && tn - 1 >= 1) issue_rows(z, tn - 1);
-                // (d) compute and send
                 const F2 W = bc(w), Gq = bc(gq), CB = bc(Cb), NK = bc(-kap), MIK = bc(-ikap),
                          ST = bc(st);
                 F2 acc = bc(0.f);
@@ -670,35 +666,20 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                             st_async1(cbase[2 * h] + ob0, ob.x, cbase[2 * h] + soff(&sm.full[z][nb]));
                             st_async1(cbase[2 * h + 1] + ob0, ob.y, cbase[2 * h + 1] + soff(&sm.full[z][nb]));
                             if (GRAD) {
-                                const uint32_t ob1 = soff(&sm.buf[z][nb][kPlanes - 1][j]);
+                                const uint32_t ob1 = ob0 + kNJ * 4;
                                 st_async1(cbase[2 * h] + ob1, bbo.x, cbase[2 * h] + soff(&sm.full[z][nb]));
                                 st_async1(cbase[2 * h + 1] + ob1, bbo.y, cbase[2 * h + 1] + soff(&sm.full[z][nb]));
                             }
                         }
                     }
                 }
-                float a = acc.x + acc.y;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-                if (t >= 0) {
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) lmin = fminf(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
-                }
-                if (lane == 0) {
-                    sm.wacc[z][warp] = a;
-                    sm.wmin[z][warp] = lmin;
-                }
-                pz = z; pnb = nb; psend = (t >= 0); ppart = true; pt = tn;
-                if (one_slot) {
-                    __syncthreads();
-                    run_tail(slot_ws);
-                }
+                float *part_row = slot_ws[z] + lay.part + ((long)tn * kCL + rank) * kWarps;
+                finish_step(z, nb, t >= 0, lmin, part_row, acc.x + acc.y, tn - 1, slot_ws);
             }
         }
         __syncthreads();
-        run_tail(slot_ws);
 
-        // Per-step partials of the four CTAs, added in a fixed order.
+        // Per-step partials of the 4 x 16 warps, added in a fixed order.
         cluster_sync();
         if (rank == 0) {
             const float scale = GRAD ? two_over_T : 1.f;
@@ -707,8 +688,14 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 if (!active[z]) continue;
                 const float *part = slot_ws[z] + lay.part;
                 for (int tn = tid; tn < N; tn += kNT) {
-                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(part + (long)tn * kCL));
-                    out[sidx[z] * N + tn] = scale * (((v.x + v.y) + v.z) + v.w);
+                    const float4 *p4 = reinterpret_cast<const float4 *>(part + (long)tn * kCL * kWarps);
+                    float sum = 0.f;
+#pragma unroll
+                    for (int i = 0; i < kCL * kWarps / 4; ++i) {
+                        const float4 v = __ldcg(p4 + i);
+                        sum += ((v.x + v.y) + v.z) + v.w;
+                    }
+                    out[sidx[z] * N + tn] = scale * sum;
                 }
             }
         }
