@@ -123,6 +123,28 @@ BCJR_API int bcjr_fb_internals(const float *seq, const float *cb, const float *T
  * `stream`): BCJR_OK, or BCJR_ERR_TIMEOUT if a bounded wait gave up. */
 BCJR_API int bcjr_ws_status(const void *ws, bcjr_stream_t stream);
 
+/*
+ * Forward without a workspace, for callers that cannot allocate device
+ * memory: a host binding this ABI from another language with no device
+ * allocator of its own, or a loop that must not call cudaMalloc between
+ * steps (cudaMalloc synchronises the device).  No counterpart in the
+ * reference (it has no C ABI); same inputs, outputs and meaning as
+ * bcjr_fb_forward.
+ *
+ * Scratch is a fixed 64 MiB array inside this library's device image, held
+ * by every GPU that loads the library until the process exits.  A shape
+ * whose single sequence slot does not fit (L=16, k=2, V=1: N above ~980) is
+ * rejected with BCJR_ERR_WORKSPACE; smaller shapes run on as many slots as
+ * fit, which is slower than bcjr_fb_forward for large batches.  The first
+ * call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make it before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  Allocates nothing, on the host or the device.
+ */
+BCJR_API int bcjr_fb_forward_noalloc(const float *seq, const float *cb, const float *T_dev,
+                                     int B, int N, int L, int k, int V,
+                                     float *soft, float *logZ, bcjr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,6 +31,7 @@ SIGNATURES = {
     "bcjr_fb_backward": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P], _I),
     "bcjr_fb_internals": ([_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P], _I),
     "bcjr_ws_status": ([_P, _P], _I),
+    "bcjr_fb_forward_noalloc": ([_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P], _I),
 }
 
 _lib = None
