@@ -11,7 +11,7 @@ Input generation follows the benchmark configs: torch.Generator seeded with
 ``seed``; the codebook is drawn first, then the weights; Student-t weights use
 numpy.random.default_rng(seed).standard_t(3) / sqrt(3).
 
-    python tests/golden/make_golden.py --ref <reference root> [--only c1|small|l16|v2]
+    python tests/golden/make_golden.py --ref <reference root> [--only c1|small|l16|v2|rht]
 """
 import argparse
 import math
@@ -104,6 +104,21 @@ def gen_v2(ref_fb):
     save("l16_v2.npz", cb=cb, w=w, grad=grad, T=np.float64(T), L=L, k=k, V=V, **out)
 
 
+def gen_rht(ref_root):
+    # RHT, sign vectors and tile order of the reference's quantizer wrapper
+    # (src/rht/transform.py:59-126, src/qat/ste.py:76-110).
+    from src.rht.transform import apply_rht, apply_inverse_rht, make_sign_vector
+    from src.qat.ste import _tile_for_viterbi
+    rng = np.random.default_rng(11)
+    W = rng.standard_normal((32, 64)).astype(np.float32)
+    sl, sr = make_sign_vector(32, 5), make_sign_vector(64, 6)
+    Wt = apply_rht(W, sl, sr)
+    Wi = apply_inverse_rht(Wt, sl, sr)
+    seqs, info = _tile_for_viterbi(Wt)
+    save("rht.npz", W=W, sign_l=sl, sign_r=sr, W_rht=Wt, W_inv=Wi, tiles=seqs,
+         info=np.array(info))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="root of the reference checkout")
@@ -112,9 +127,12 @@ def main():
     sys.path.insert(0, args.ref)
     from src.bcjr.forward_backward import bcjr_forward_backward as ref_fb
     torch.set_num_threads(os.cpu_count() or 1)
-    todo = [args.only] if args.only else ["small", "c1", "v2", "l16"]
+    todo = [args.only] if args.only else ["small", "c1", "v2", "l16", "rht"]
     for what in todo:
-        {"c1": gen_c1, "small": gen_small, "l16": gen_l16, "v2": gen_v2}[what](ref_fb)
+        if what == "rht":
+            gen_rht(args.ref)
+        else:
+            {"c1": gen_c1, "small": gen_small, "l16": gen_l16, "v2": gen_v2}[what](ref_fb)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,106 @@
+"""Caller-side layer (quant_2bit_b200.quant, .hook): RHT, sign vectors and
+tile order against the reference's outputs (tests/golden/rht.npz), the hook
+against an importable reference checkout, and (GPU) the whole quantizer
+wrapper against the reference's eager algorithm on CPU."""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle import torch_port
+
+
+def _rht():
+    return dict(np.load(os.path.join(GOLDEN, "rht.npz")))
+
+
+def test_sign_vectors_match_reference():
+    from quant_2bit_b200.quant import make_sign_vector
+    d = _rht()
+    np.testing.assert_array_equal(make_sign_vector(32, 5), d["sign_l"])
+    np.testing.assert_array_equal(make_sign_vector(64, 6), d["sign_r"])
+
+
+def test_rht_and_inverse_match_reference():
+    from quant_2bit_b200.quant import apply_inverse_rht_gpu, apply_rht_gpu
+    d = _rht()
+    W = torch.tensor(d["W"])
+    sl, sr = torch.tensor(d["sign_l"]), torch.tensor(d["sign_r"])
+    Wt = apply_rht_gpu(W, sl, sr)
+    np.testing.assert_allclose(Wt.numpy(), d["W_rht"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(apply_inverse_rht_gpu(torch.tensor(d["W_rht"]), sl, sr).numpy(),
+                               d["W_inv"], rtol=1e-5, atol=1e-6)
+
+
+def test_tile_order_matches_reference_and_round_trips():
+    from quant_2bit_b200.quant import _tile_for_viterbi_gpu, _untile_from_viterbi_gpu
+    d = _rht()
+    # the reference tiles in float32 (src/qat/ste.py:96-98)
+    Wt = torch.tensor(d["W_rht"].astype(np.float32))
+    seqs, info = _tile_for_viterbi_gpu(Wt)
+    np.testing.assert_array_equal(seqs.numpy(), d["tiles"])
+    assert tuple(info) == tuple(d["info"])
+    assert torch.equal(_untile_from_viterbi_gpu(seqs, info, Wt.shape), Wt)
+
+
+def test_hook_patches_reference_modules():
+    ref = os.environ.get("QUANT2BIT_REFERENCE", "/root/reference")
+    if not os.path.isdir(os.path.join(ref, "src", "bcjr")):
+        pytest.skip("reference checkout not present")
+    sys.path.insert(0, ref)
+    try:
+        import src.bcjr.bcjr_quant as bq
+        import src.qat.ste as ste
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"reference not importable: {e}")
+    import quant_2bit_b200.hook as hook
+    from quant_2bit_b200 import quant
+    orig = bq._bcjr_chunk_forward
+    try:
+        names = hook.install()
+        assert "src.bcjr.bcjr_quant._bcjr_chunk_forward" in names
+        assert bq._bcjr_chunk_forward is quant._bcjr_chunk_forward
+        assert bq.bcjr_quantize_tiles is quant.bcjr_quantize_tiles
+        if not getattr(ste, "_HAS_FHT", False):
+            assert bq.apply_rht_gpu is quant.apply_rht_gpu
+    finally:
+        hook.uninstall()
+    assert bq._bcjr_chunk_forward is orig
+
+
+@pytest.mark.gpu
+def test_quantize_weight_matches_reference_pipeline(cuda_ok):
+    """bcjr_quantize_weight (RHT -> RMS scale -> tile -> BCJR -> untile ->
+    inverse RHT) and its gradient, against the same pipeline built on the
+    reference's eager BCJR (torch port, fp64, CPU)."""
+    from quant_2bit_b200 import quant
+    L, k, V, T = 8, 2, 1, 0.6
+    rng = np.random.default_rng(3)
+    W = rng.standard_normal((32, 64)).astype(np.float32)
+    cb = rng.standard_normal((1 << L, V)).astype(np.float32)
+    sl, sr = quant.make_sign_vector(32, 1), quant.make_sign_vector(64, 2)
+    G = rng.standard_normal((32, 64)).astype(np.float32)
+
+    dev = torch.device("cuda")
+    Wd = torch.tensor(W, device=dev, requires_grad=True)
+    Wq = quant.bcjr_quantize_weight(Wd, torch.tensor(sl, device=dev), torch.tensor(sr, device=dev),
+                                    torch.tensor(cb, device=dev),
+                                    torch.tensor(T, device=dev))
+    (Wq * torch.tensor(G, device=dev)).sum().backward()
+
+    Wr = torch.tensor(W, dtype=torch.float64, requires_grad=True)
+    s_l, s_r = torch.tensor(sl, dtype=torch.float64), torch.tensor(sr, dtype=torch.float64)
+    Wt = quant.apply_rht_gpu(Wr, s_l, s_r)
+    scale = Wt.detach().pow(2).mean().sqrt()
+    seqs, info = quant._tile_for_viterbi_gpu(Wt / scale)
+    soft, _ = torch_port.bcjr_forward_backward(seqs.reshape(seqs.shape[0], -1, V),
+                                               torch.tensor(cb, dtype=torch.float64), T, L, k, V)
+    Wq_ref = quant.apply_inverse_rht_gpu(
+        quant._untile_from_viterbi_gpu(soft.reshape(seqs.shape), info, W.shape) * scale, s_l, s_r)
+    (Wq_ref * torch.tensor(G, dtype=torch.float64)).sum().backward()
+    np.testing.assert_allclose(Wq.detach().cpu().numpy(), Wq_ref.detach().numpy(),
+                               rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(Wd.grad.cpu().numpy(), Wr.grad.numpy(), rtol=1e-4, atol=1e-5)
