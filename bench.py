@@ -46,6 +46,11 @@ STATE_STEPS_PER_SEQ = NSTEP * (1 << L)
 # backward (7.5 per fwd+bwd state-step).
 MUFU_FWD, MUFU_BWD = 3.5, 4.0
 MUFU_PER_SM_CLK = 16
+# dram__bytes_read.sum + dram__bytes_write.sum per sequence of the cluster
+# kernels (L=16, N=256), from one ncu capture of a 148-sequence launch
+# (profiles/bcjr_l16_config2.md); traffic grows in proportion to sequences.
+DRAM_BYTES_PER_SEQ = {"forward": (2.222191e9 + 2.488541e9) / 148,
+                      "backward": (4.726516e9 + 4.964882e9) / 148}
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -359,7 +364,10 @@ def main():
             "gpu_launches": 2 * args.steps,
             "kernel_ms": {"forward": fwd_avg, "backward": bwd_avg},
             "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak,
-                         "unit": "Gop/s", "frac": achieved / peak, "traffic": None,
+                         "unit": "Gop/s", "frac": achieved / peak,
+                         "traffic": DRAM_BYTES_PER_SEQ[dom] * Bl,
+                         "traffic_unit": "bytes per launch (ncu, 148-sequence capture scaled by "
+                                         "sequences; see profiles/)",
                          "note": f"algorithmic MUFU ops: {MUFU_FWD}/{MUFU_BWD} per state-step "
                                  f"(fwd/bwd call), peak = {sms} SMs x 16/clk x {clk_mhz:.0f} MHz"},
             "e2e": {"value": e2e_value, "unit": UNIT,
