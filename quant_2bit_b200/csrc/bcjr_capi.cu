@@ -88,6 +88,10 @@ int prepare(bcjr::LaunchArgs &a, void *ws, size_t ws_bytes, int mode) {
     a.ws_data_bytes = ws_bytes - kHeaderBytes;
     a.mode = mode;
     a.fast = use_l16(a.B, a.N, a.L, a.BB, a.V, mode);
+    // Test-only: BCJR_B200_TEST_DROP_SENDS=1 makes the cluster kernel's CTA 1
+    // withhold its outputs so that the bounded waits time out (tests/ only).
+    const char *drop = std::getenv("BCJR_B200_TEST_DROP_SENDS");
+    a.drop_sends = (drop && drop[0] == '1') ? 1 : 0;
     a.grid = a.fast ? 1 : bcjr::generic_grid(a.B, a.N, a.L, a.BB, mode, a.ws_data_bytes);
     if (a.grid < 1) return BCJR_ERR_WORKSPACE;
     if (cudaMemsetAsync(a.status, 0, sizeof(int), a.stream) != cudaSuccess) return BCJR_ERR_LAUNCH;

@@ -21,6 +21,7 @@ struct LaunchArgs {
     int mode;
     int grid;
     bool fast;                    // cluster kernel (bcjr_l16.cu)
+    int drop_sends;               // test-only fault injection (cluster kernel)
     cudaStream_t stream;
 };
 

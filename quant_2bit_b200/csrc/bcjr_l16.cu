@@ -86,6 +86,7 @@ struct alignas(128) Smem {
     unsigned long long hbar[kSlots];
     int mn[kSlots][2];                    // per-step CTA minimum (order-preserving int key)
     int cnt[kSlots][2];                   // warps finished with the step
+    int hiss[kSlots];                     // TMA row loads issued per slot
 };
 
 // ---------------------------------------------------------------------------
@@ -246,7 +247,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
            const float *__restrict__ T_dev, const float *__restrict__ soft_in,
            const float *__restrict__ grad, int B, int N,
            float *__restrict__ out, float *__restrict__ logZ_out,
-           float *__restrict__ ws, int *status) {
+           float *__restrict__ ws, int *status, int drop_sends) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     using SM = Smem<GRAD>;
     SM &sm = *reinterpret_cast<SM *>(smem_raw);
@@ -308,11 +309,13 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     }
 
     if (tid == 0) {
-        for (int z = 0; z < kSlots; ++z)
+        for (int z = 0; z < kSlots; ++z) {
+            sm.hiss[z] = 0;
             for (int x = 0; x < 2; ++x) {
                 sm.mn[z][x] = order_key(kPosInf);
                 sm.cnt[z][x] = 0;
             }
+        }
         for (int z = 0; z < kSlots; ++z) {
             for (int x = 0; x < 2; ++x) mbar_init(sbase + soff(&sm.full[z][x]), 1);
             mbar_init(sbase + soff(&sm.hbar[z]), 1);
@@ -322,6 +325,9 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     cluster_sync();
 
     bool failed = false;
+    // Test-only fault injection (BCJR_B200_TEST_DROP_SENDS): CTA rank 1 never
+    // sends its alpha-sweep outputs, so every consumer's bounded wait expires.
+    const bool drop = drop_sends != 0 && rank == 1;
     uint32_t use[kSlots] = {0, 0};    // ring consumptions per slot (uniform over the CTA)
     uint32_t hcnt[kSlots] = {0, 0};   // TMA row loads waited per slot
 
@@ -335,6 +341,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     auto issue_rows = [&](int z, int tn, float *const *slot_ws) {
         const uint32_t hb = sbase + soff(&sm.hbar[z]);
         if (failed) return;
+        atomicAdd(&sm.hiss[z], 1);
         mbar_arm(hb, kPlanes * kNJ * 4);
         const float *hist = slot_ws[z] + lay.hist + (long)tn * kG + rank * kJPC;
 #pragma unroll
@@ -350,10 +357,8 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 
     auto finish_step = [&](int z, int nb, bool send, float lmin, float *part_row, float acc,
                            int rows_tn, float *const *slot_ws) {
-        if (send) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) lmin = fminf(lmin, __shfl_xor_sync(0xffffffffu, lmin, o));
-        }
+        // warp minimum with one redux.sync on the order-preserving integer key
+        const int wkey = send ? __reduce_min_sync(0xffffffffu, order_key(lmin)) : 0;
         if (part_row) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -361,7 +366,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         int last = 0;
         if (lane == 0) {
             if (part_row) part_row[warp] = acc;
-            if (send) atomicMin(&sm.mn[z][nb], order_key(lmin));
+            if (send) atomicMin(&sm.mn[z][nb], wkey);
             __threadfence_block();
             last = atomicAdd(&sm.cnt[z][nb], 1) == kWarps - 1;
         }
@@ -449,6 +454,8 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     gs = gq * sm.sf[z][t];
                 }
                 const bool last = (t == N - 1);
+                const uint32_t bar_off = soff(&sm.full[z][nb]);
+                const uint32_t buf_off = soff(&sm.buf[z][nb][0][0]);
                 const F2 W = bc(w), Gq = bc(gq), GS = bc(-gs), NK = bc(-kap);
                 float lmin = kPosInf;
                 float *hist = slot_ws[z] + lay.hist + (long)(t + 1) * kG;
@@ -478,9 +485,9 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     lmin = fminf(lmin, min4(o4[0], o4[1], o4[2], o4[3]));
                     const int j = jg[jj];
                     if (!last) {
-                        const uint32_t bar = rdst[jj] + soff(&sm.full[z][nb]);
-                        const uint32_t o0 = rdst[jj] + soff(&sm.buf[z][nb][0][0]) + aoff[jj];
-                        if (!failed) {
+                        const uint32_t bar = rdst[jj] + bar_off;
+                        const uint32_t o0 = rdst[jj] + buf_off + aoff[jj];
+                        if (!failed && !drop) {
                             st_async4(o0, o4[0], o4[1], o4[2], o4[3], bar);
                             if (GRAD)
                                 st_async4(o0 + kNJ * 4, h4[0], h4[1], h4[2], h4[3], bar);
@@ -493,7 +500,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                         for (int c = 0; c < 4; ++c) smin_merge(lzm[z], lzs[z], kap * o4[c], 1.f);
                     }
                 }
-                finish_step(z, nb, !last, lmin, nullptr, 0.f, 0, slot_ws);
+                finish_step(z, nb, !last && !drop, lmin, nullptr, 0.f, 0, slot_ws);
             }
         }
         __syncthreads();
@@ -615,6 +622,8 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     st = sm.sf[z][tn];
                     gs = gq * st;
                 }
+                const uint32_t bar_off = soff(&sm.full[z][nb]);
+                const uint32_t buf_off = soff(&sm.buf[z][nb][0][0]);
                 const F2 W = bc(w), Gq = bc(gq), CB = bc(Cb), NK = bc(-kap), MIK = bc(-ikap),
                          ST = bc(st);
                 F2 acc = bc(0.f);
@@ -662,13 +671,13 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                             acc = fma2(f, dl, acc);
                         }
                         if (t >= 0 && !failed) {
-                            const uint32_t ob0 = soff(&sm.buf[z][nb][0][j]);
-                            st_async1(cbase[2 * h] + ob0, ob.x, cbase[2 * h] + soff(&sm.full[z][nb]));
-                            st_async1(cbase[2 * h + 1] + ob0, ob.y, cbase[2 * h + 1] + soff(&sm.full[z][nb]));
+                            const uint32_t ob0 = buf_off + 4u * (uint32_t)j;
+                            st_async1(cbase[2 * h] + ob0, ob.x, cbase[2 * h] + bar_off);
+                            st_async1(cbase[2 * h + 1] + ob0, ob.y, cbase[2 * h + 1] + bar_off);
                             if (GRAD) {
                                 const uint32_t ob1 = ob0 + kNJ * 4;
-                                st_async1(cbase[2 * h] + ob1, bbo.x, cbase[2 * h] + soff(&sm.full[z][nb]));
-                                st_async1(cbase[2 * h + 1] + ob1, bbo.y, cbase[2 * h + 1] + soff(&sm.full[z][nb]));
+                                st_async1(cbase[2 * h] + ob1, bbo.x, cbase[2 * h] + bar_off);
+                                st_async1(cbase[2 * h + 1] + ob1, bbo.y, cbase[2 * h + 1] + bar_off);
                             }
                         }
                     }
@@ -699,6 +708,16 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 }
             }
         }
+    }
+    // No CTA leaves with a TMA row copy in flight (only possible after a
+    // failure): wait, bounded, for every issued load that was not consumed.
+    __syncthreads();
+    if (tid == 0) {
+        bool f2 = false;
+#pragma unroll
+        for (int z = 0; z < kSlots; ++z)
+            for (uint32_t k = hcnt[z]; k < (uint32_t)sm.hiss[z]; ++k)
+                wait_bar(sbase + soff(&sm.hbar[z]), k & 1, status, f2);
     }
     cluster_sync();
 }
@@ -775,10 +794,12 @@ cudaError_t launch_l16(const LaunchArgs &a) {
     float *ws = reinterpret_cast<float *>(a.ws_data);
     if (grad) {
         l16::l16_kernel<true><<<grid, block, sizeof(l16::Smem<true>), a.stream>>>(
-            a.seq, a.cb, a.T_dev, a.soft_in, a.grad, a.B, a.N, a.dseq, nullptr, ws, a.status);
+            a.seq, a.cb, a.T_dev, a.soft_in, a.grad, a.B, a.N, a.dseq, nullptr, ws, a.status,
+            a.drop_sends);
     } else {
         l16::l16_kernel<false><<<grid, block, sizeof(l16::Smem<false>), a.stream>>>(
-            a.seq, a.cb, a.T_dev, nullptr, nullptr, a.B, a.N, a.soft, a.logZ, ws, a.status);
+            a.seq, a.cb, a.T_dev, nullptr, nullptr, a.B, a.N, a.soft, a.logZ, ws, a.status,
+            a.drop_sends);
     }
     return cudaGetLastError();
 }

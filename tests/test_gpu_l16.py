@@ -85,3 +85,32 @@ def test_low_temperature_normwise(cuda_ok):
         np.testing.assert_allclose(s, s64, rtol=1e-4, atol=1e-5)
         assert np.abs(d - d64).max() / np.abs(d64).max() < 1e-4
         np.testing.assert_allclose(z, z64, rtol=2e-6)
+
+
+def test_bounded_wait_timeout_is_reported_and_context_survives(cuda_ok):
+    """Failure detection without a GPU fault: with BCJR_B200_TEST_DROP_SENDS=1
+    one CTA of each cluster withholds its outputs, every consumer's bounded
+    wait (~1 s) expires, the kernel records BCJR_ERR_TIMEOUT in the workspace
+    status word and finishes; the host reads the status, and the next normal
+    call on the same context is correct."""
+    from quant_2bit_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(4)
+    cb = torch.tensor(rng.standard_normal((65536, 1)), dtype=torch.float32, device=dev)
+    w = torch.tensor(rng.standard_normal((2, 8, 1)), dtype=torch.float32, device=dev)
+    T = torch.tensor(0.5, device=dev)
+    soft = torch.empty_like(w)
+    ws = _lib.workspace(2, 8, 16, 2, 1, _lib.WS_FORWARD, dev)
+    P, sp = _lib.ptr, _lib.stream_ptr(dev)
+    os.environ["BCJR_B200_TEST_DROP_SENDS"] = "1"
+    try:
+        rc = lib.bcjr_fb_forward(P(w), P(cb), P(T), 2, 8, 16, 2, 1, P(soft), None,
+                                 P(ws), ws.numel(), sp)
+    finally:
+        del os.environ["BCJR_B200_TEST_DROP_SENDS"]
+    assert rc == 0
+    assert lib.bcjr_ws_status(P(ws), sp) == _lib.BCJR_ERR_TIMEOUT
+    s1, _, _ = _run(w.cpu().numpy(), cb.cpu().numpy(), 0.5, np.ones((2, 8, 1), np.float32))
+    s64, _, _ = oracle.fb(w.cpu().numpy(), cb.cpu().numpy(), 0.5, 16, 2, 1)
+    np.testing.assert_allclose(s1, s64, rtol=1e-4, atol=1e-5)
