@@ -1,7 +1,7 @@
 """Benchmark: BCJR forward+backward state-transitions/sec on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c5]
+                    [--config c2|c3|c5] [--temperature T] [--weights gauss|t3]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, NCCL)
 
 Workload (synthetic, seeded): L=16, k=2, V=1, N=256 steps,
@@ -29,6 +29,7 @@ import sys
 import tempfile
 import time
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -71,13 +72,18 @@ def tile(W, Tx=16, Ty=16):
     return W.view(m, n // Ty, Ty).permute(1, 0, 2).reshape((m // Tx) * (n // Ty), Tx * Ty)
 
 
-def make_inputs(config, rank, world):
-    """Codebook (65536, 1) and this rank's sequences (B_local, 256, 1), on CPU."""
+def make_inputs(config, rank, world, weights="gauss"):
+    """Codebook (65536, 1) and this rank's sequences (B_local, 256, 1), on CPU.
+    weights="t3": config 4's heavy-tailed variant, Student-t(3)/sqrt(3) drawn
+    with numpy.random.default_rng(seed) in place of the N(0,1) draws."""
     g = torch.Generator().manual_seed(0)
     cb = torch.randn(1 << L, 1, generator=g)
     if config == "c2":
         gw = torch.Generator().manual_seed(1000 + rank) if rank else g
         w = torch.randn(4096, NSTEP, 1, generator=gw)
+        if weights == "t3":
+            w = torch.tensor(np.random.default_rng(rank).standard_t(3, size=(4096, NSTEP, 1))
+                             / math.sqrt(3.0), dtype=torch.float32)
         return cb, w, 4096 * world
     shapes = llama_layer_shapes() if config == "c3" else olmoe_layer_shapes()
     total = sum((m // 16) * (n // 16) for m, n in shapes)
@@ -160,15 +166,15 @@ def cpu_reference(args, rank):
     from oracle import torch_port
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cb, w, _ = make_inputs("c2" if args.config == "c2" else args.config, 0, 1)
+    cb, w, _ = make_inputs(args.config, 0, 1, args.weights)
     nseq = args.cpu_sample_seqs
     sample = w[:nseq]
     for _ in range(args.warmup if args.impl == "reference" else 0):
-        torch_port.fwd_bwd(sample, cb, TEMP, L, K_BITS, V, chunk=8)
+        torch_port.fwd_bwd(sample, cb, args.temperature, L, K_BITS, V, chunk=8)
     t0 = time.perf_counter()
     steps = args.steps if args.impl == "reference" else 1
     for _ in range(steps):
-        torch_port.fwd_bwd(sample, cb, TEMP, L, K_BITS, V, chunk=8)
+        torch_port.fwd_bwd(sample, cb, args.temperature, L, K_BITS, V, chunk=8)
     dt = (time.perf_counter() - t0) / steps
     value = nseq * EDGES_PER_SEQ / dt
     return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
@@ -184,6 +190,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5"])
+    ap.add_argument("--temperature", type=float, default=TEMP,
+                    help="T (config 4 sweeps 4, 2, 1, 0.5, 0.25, 0.1, 0.05)")
+    ap.add_argument("--weights", default="gauss", choices=["gauss", "t3"],
+                    help="config 4's Student-t(3) weights with --config c2")
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sequences", type=int, default=0,
@@ -205,7 +215,8 @@ def main():
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic (seeded randn, BASELINE configs)",
                 "impl": "reference",
-                "config": {"workload": f"{args.config}: L=16 k=2 V=1 N=256 T=0.5, CPU sample",
+                "config": {"workload": f"{args.config}: L=16 k=2 V=1 N=256 T={args.temperature:g} "
+                                       f"{args.weights} weights, CPU sample",
                            "sample_sequences": args.cpu_sample_seqs},
                 "cpu_baseline": ref,
                 "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -222,14 +233,14 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
-    cb_cpu, w_cpu, total_seqs = make_inputs(args.config, rank, world)
+    cb_cpu, w_cpu, total_seqs = make_inputs(args.config, rank, world, args.weights)
     if args.sequences:
         w_cpu = w_cpu[:args.sequences].contiguous()
         total_seqs = w_cpu.shape[0] * world
     cb = cb_cpu.to(dev)
     w = w_cpu.to(dev)
     Bl = w.shape[0]
-    T = torch.tensor(TEMP, dtype=torch.float32, device=dev)
+    T = torch.tensor(args.temperature, dtype=torch.float32, device=dev)
     soft = torch.empty((Bl, NSTEP, V), device=dev)
     logZ = torch.empty((Bl,), device=dev)
     grad = torch.ones((Bl, NSTEP, V), device=dev)
@@ -356,7 +367,8 @@ def main():
             "config": {"workload": {"c2": "config 2: one 1024x1024 weight per GPU",
                                     "c3": "config 3: Llama-3.2-1B layer, sharded",
                                     "c5": "config 5: OLMoE MoE layer, sharded"}[args.config]
-                       + " (L=16, k=2, V=1, N=256, T=0.5, fwd+bwd, grad=ones)",
+                       + f" (L=16, k=2, V=1, N=256, T={args.temperature:g}, {args.weights} weights,"
+                         " fwd+bwd, grad=ones)",
                        "sequences_per_gpu": Bl, "sequences_total": Bl * world if (args.config == "c2" or args.sequences) else total_seqs,
                        "l2": "flushed between timed steps (256 MB write, outside the events)",
                        "collective": "NCCL all_gather of soft per step" if world > 1 else "none"},

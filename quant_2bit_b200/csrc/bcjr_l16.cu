@@ -204,6 +204,13 @@ __device__ __forceinline__ float min4(float a, float b, float c, float d) {
 }
 __device__ __forceinline__ F2 ex2p(F2 a) { return F2{ex2(a.x), ex2(a.y)}; }
 
+// Minimum over the warp (all 32 lanes active).
+__device__ __forceinline__ float redux_min(float v) {
+    float r;
+    asm volatile("redux.sync.min.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    return r;
+}
+
 // Order-preserving map float -> int (and back): a < b  <=>  key(a) < key(b).
 __device__ __forceinline__ int order_key(float f) {
     const int i = __float_as_int(f);
@@ -358,7 +365,8 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     auto finish_step = [&](int z, int nb, bool send, float lmin, float *part_row, float acc,
                            int rows_tn, float *const *slot_ws) {
         // warp minimum with one redux.sync on the order-preserving integer key
-        const int wkey = send ? __reduce_min_sync(0xffffffffu, order_key(lmin)) : 0;
+        // warp minimum with one float redux.sync (sm_100a); integer key for the smem atomic
+        const float wmin = send ? redux_min(lmin) : 0.f;
         if (part_row) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -366,7 +374,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         int last = 0;
         if (lane == 0) {
             if (part_row) part_row[warp] = acc;
-            if (send) atomicMin(&sm.mn[z][nb], wkey);
+            if (send) atomicMin(&sm.mn[z][nb], order_key(wmin));
             __threadfence_block();
             last = atomicAdd(&sm.cnt[z][nb], 1) == kWarps - 1;
         }
@@ -641,7 +649,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                         }
                         const F2 M = mk(min4(xc[0].x, xc[1].x, xc[2].x, xc[3].x),
                                         min4(xc[0].y, xc[1].y, xc[2].y, xc[3].y));
-                        const F2 KM = mk(kap * M.x, kap * M.y);
+                        const F2 KM = mul2(M, bc(kap));
                         F2 e[4];
 #pragma unroll
                         for (int c = 0; c < 4; ++c) e[c] = ex2p(fma2(xc[c], NK, KM));
