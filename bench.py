@@ -1,7 +1,7 @@
 """Benchmark: BCJR forward+backward state-transitions/sec on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c5] [--temperature T] [--weights gauss|t3]
+                    [--config c2|c3|c5|v2] [--temperature T] [--weights gauss|t3]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, NCCL)
 
 Workload (synthetic, seeded): L=16, k=2, V=1, N=256 steps,
@@ -14,6 +14,9 @@ T=0.5, codebook randn(65536) (seed 0), weights randn drawn after the codebook.
   all-gathered.
 * c5: the OLMoE-shaped MoE layer (1,572,864 sequences), experts sharded
   8 per GPU at N=8 (strong scaling).
+* v2: the shape the reference's QAT layers use, k=2, V=2 (b = 4, 16
+  predecessors per state), N=128: one 1024x1024 weight = 4,096 sequences of
+  128 two-dimensional steps per GPU, codebook randn(65536, 2).
 
 One step = forward (soft) + backward (d_seq for an upstream gradient of ones)
 of every local sequence (+ the all-gather when N > 1).  One transition = one
@@ -38,20 +41,21 @@ sys.path.insert(0, ROOT)
 
 METRIC = "BCJR fwd+bwd state-transitions/sec (L=16,k=2) at 1/2/4/8 B200; % MUFU roofline"
 UNIT = "transitions/s"
-L, K_BITS, V, NSTEP, TEMP = 16, 2, 1, 256, 0.5
-EDGES_PER_SEQ = NSTEP * (1 << L) * (1 << (K_BITS * V))
-STATE_STEPS_PER_SEQ = NSTEP * (1 << L)
+L, K_BITS, TEMP = 16, 2, 0.5
+# (V, N) per config
+SHAPES = {"c2": (1, 256), "c3": (1, 256), "c5": (1, 256), "v2": (2, 128)}
 # Algorithmic MUFU (ex2/lg2/rcp) per state-step, forward call and backward
-# call, at kV = 2: alpha LSE 5/4 + beta LSE 5/4 + marginal exp 1 = 3.5 for the
-# forward; the same recompute plus 2/2^b softmax normalisers = 4.0 for the
-# backward (7.5 per fwd+bwd state-step).
-MUFU_FWD, MUFU_BWD = 3.5, 4.0
+# call: alpha LSE (2^b+1)/2^b + beta LSE (2^b+1)/2^b + marginal exp 1 for the
+# forward; the same recompute plus 2/2^b softmax normalisers for the
+# backward.  b = 2: 3.5 + 4.0 = 7.5; b = 4: 3.125 + 3.25 = 6.375.
+MUFU = {1: (3.5, 4.0), 2: (3.125, 3.25)}
 MUFU_PER_SM_CLK = 16
 # dram__bytes_read.sum + dram__bytes_write.sum per sequence of the cluster
-# kernels (L=16, N=256), from one ncu capture of a 148-sequence launch
-# (profiles/bcjr_l16_config2.md); traffic grows in proportion to sequences.
-DRAM_BYTES_PER_SEQ = {"forward": (2.222191e9 + 2.488541e9) / 148,
-                      "backward": (4.726516e9 + 4.964882e9) / 148}
+# kernels from one ncu capture of a 148-sequence launch (profiles/); traffic
+# grows in proportion to sequences.  V=1: L=16, N=256.
+DRAM_BYTES_PER_SEQ = {1: {"forward": (2.222191e9 + 2.488541e9) / 148,
+                          "backward": (4.726516e9 + 4.964882e9) / 148},
+                      2: None}
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -73,16 +77,17 @@ def tile(W, Tx=16, Ty=16):
 
 
 def make_inputs(config, rank, world, weights="gauss"):
-    """Codebook (65536, 1) and this rank's sequences (B_local, 256, 1), on CPU.
+    """Codebook (65536, V) and this rank's sequences (B_local, N, V), on CPU.
     weights="t3": config 4's heavy-tailed variant, Student-t(3)/sqrt(3) drawn
     with numpy.random.default_rng(seed) in place of the N(0,1) draws."""
+    V, NSTEP = SHAPES[config]
     g = torch.Generator().manual_seed(0)
-    cb = torch.randn(1 << L, 1, generator=g)
-    if config == "c2":
+    cb = torch.randn(1 << L, V, generator=g)
+    if config in ("c2", "v2"):
         gw = torch.Generator().manual_seed(1000 + rank) if rank else g
-        w = torch.randn(4096, NSTEP, 1, generator=gw)
+        w = torch.randn(4096, NSTEP, V, generator=gw)
         if weights == "t3":
-            w = torch.tensor(np.random.default_rng(rank).standard_t(3, size=(4096, NSTEP, 1))
+            w = torch.tensor(np.random.default_rng(rank).standard_t(3, size=(4096, NSTEP, V))
                              / math.sqrt(3.0), dtype=torch.float32)
         return cb, w, 4096 * world
     shapes = llama_layer_shapes() if config == "c3" else olmoe_layer_shapes()
@@ -103,7 +108,7 @@ def make_inputs(config, rank, world, weights="gauss"):
             a, b_ = max(lo, off) - off, min(hi, off + cnt) - off
             seqs.append(t[a:b_])
         off += cnt
-    w = torch.cat(seqs).view(-1, NSTEP, 1).contiguous()
+    w = torch.cat(seqs).view(-1, NSTEP, V).contiguous()
     return cb, w, total
 
 
@@ -164,6 +169,8 @@ def cpu_reference(args, rank):
     the host's CPU cores: one forward + backward of a bounded sample of the
     same workload per step."""
     from oracle import torch_port
+    V, NSTEP = SHAPES[args.config]
+    edges_per_seq = NSTEP * (1 << L) * (1 << (K_BITS * V))
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     cb, w, _ = make_inputs(args.config, 0, 1, args.weights)
@@ -176,9 +183,9 @@ def cpu_reference(args, rank):
     for _ in range(steps):
         torch_port.fwd_bwd(sample, cb, args.temperature, L, K_BITS, V, chunk=8)
     dt = (time.perf_counter() - t0) / steps
-    value = nseq * EDGES_PER_SEQ / dt
+    value = nseq * edges_per_seq / dt
     return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{nseq} sequence(s) of {args.config} (L=16, N=256), fwd + bwd with "
+            "sample": f"{nseq} sequence(s) of {args.config} (L=16, V={V}, N={NSTEP}), fwd + bwd with "
                       f"grad=ones, chunk 8, torch {torch.__version__} CPU, "
                       f"{threads} threads, {dt:.2f} s per step"}
 
@@ -189,7 +196,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5", "v2"])
     ap.add_argument("--temperature", type=float, default=TEMP,
                     help="T (config 4 sweeps 4, 2, 1, 0.5, 0.25, 0.1, 0.05)")
     ap.add_argument("--weights", default="gauss", choices=["gauss", "t3"],
@@ -201,6 +208,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
 
+    V, NSTEP = SHAPES[args.config]
+    EDGES_PER_SEQ = NSTEP * (1 << L) * (1 << (K_BITS * V))
+    STATE_STEPS_PER_SEQ = NSTEP * (1 << L)
+    MUFU_FWD, MUFU_BWD = MUFU[V]
+    weak = args.config in ("c2", "v2")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -215,7 +227,7 @@ def main():
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic (seeded randn, BASELINE configs)",
                 "impl": "reference",
-                "config": {"workload": f"{args.config}: L=16 k=2 V=1 N=256 T={args.temperature:g} "
+                "config": {"workload": f"{args.config}: L=16 k=2 V={V} N={NSTEP} T={args.temperature:g} "
                                        f"{args.weights} weights, CPU sample",
                            "sample_sequences": args.cpu_sample_seqs},
                 "cpu_baseline": ref,
@@ -306,7 +318,7 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t_max_ms = float(t.item())
-    edges_total = (Bl * world if args.config == "c2" or args.sequences else total_seqs) * EDGES_PER_SEQ
+    edges_total = (Bl * world if weak or args.sequences else total_seqs) * EDGES_PER_SEQ
     value = edges_total * args.steps / (t_max_ms / 1e3)
 
     # e2e: the public autograd API with host buffers, H2D and D2H in the timed region.
@@ -361,15 +373,16 @@ def main():
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak" if args.config == "c2" else "strong",
+            "higher_is_better": True, "scaling": "weak" if weak else "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded randn codebook and weights, BASELINE configs)",
             "config": {"workload": {"c2": "config 2: one 1024x1024 weight per GPU",
                                     "c3": "config 3: Llama-3.2-1B layer, sharded",
-                                    "c5": "config 5: OLMoE MoE layer, sharded"}[args.config]
-                       + f" (L=16, k=2, V=1, N=256, T={args.temperature:g}, {args.weights} weights,"
+                                    "c5": "config 5: OLMoE MoE layer, sharded",
+                                    "v2": "b=4 (k=2, V=2): one 1024x1024 weight per GPU"}[args.config]
+                       + f" (L=16, k=2, V={V}, N={NSTEP}, T={args.temperature:g}, {args.weights} weights,"
                          " fwd+bwd, grad=ones)",
-                       "sequences_per_gpu": Bl, "sequences_total": Bl * world if (args.config == "c2" or args.sequences) else total_seqs,
+                       "sequences_per_gpu": Bl, "sequences_total": Bl * world if (weak or args.sequences) else total_seqs,
                        "l2": "flushed between timed steps (256 MB write, outside the events)",
                        "collective": "NCCL all_gather of soft per step" if world > 1 else "none"},
             "clocks": clk,
@@ -377,7 +390,7 @@ def main():
             "kernel_ms": {"forward": fwd_avg, "backward": bwd_avg},
             "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "Gop/s", "frac": achieved / peak,
-                         "traffic": DRAM_BYTES_PER_SEQ[dom] * Bl,
+                         "traffic": DRAM_BYTES_PER_SEQ[V][dom] * Bl if DRAM_BYTES_PER_SEQ[V] else None,
                          "traffic_unit": "bytes per launch (ncu, 148-sequence capture scaled by "
                                          "sequences; see profiles/)",
                          "note": f"algorithmic MUFU ops: {MUFU_FWD}/{MUFU_BWD} per state-step "

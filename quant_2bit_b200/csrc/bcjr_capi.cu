@@ -60,19 +60,39 @@ int check_shape(int B, int N, int L, int k, int V) {
 
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// The cluster kernel serves L=16, k=2, V=1 (forward and backward); every
-// other shape, the internals, and BCJR_B200_FORCE_GENERIC=1 take the generic
-// kernels.
-bool use_l16(int B, int N, int L, int b, int V, int mode) {
-    if (mode == bcjr::kModeInternals) return false;
+// Kernel choice.  The cluster kernels serve L=16, k=2 with V=1 (bcjr_l16.cu)
+// and V=2 (bcjr_b4.cu), forward and backward, for 2 <= N <= 512; they read
+// the codebook with 16-byte vector loads, so a codebook pointer that is not
+// 16-byte aligned (a view at an odd offset) takes the generic kernels, as do
+// every other shape, the internals, and BCJR_B200_FORCE_GENERIC=1.
+int pick_kernel(int B, int N, int L, int b, int V, int mode, const void *cb) {
+    if (mode == bcjr::kModeInternals) return bcjr::kKernelGeneric;
     const char *env = std::getenv("BCJR_B200_FORCE_GENERIC");
-    if (env && env[0] == '1') return false;
-    return bcjr::l16_applicable(B, N, L, b, V) && bcjr::l16_clusters(B, mode) > 0;
+    if (env && env[0] == '1') return bcjr::kKernelGeneric;
+    if (cb && !aligned(cb, 16)) return bcjr::kKernelGeneric;
+    if (bcjr::l16_applicable(B, N, L, b, V) && bcjr::l16_clusters(B, mode) > 0)
+        return bcjr::kKernelL16;
+    if (bcjr::b4_applicable(B, N, L, b, V) && bcjr::b4_clusters(B, mode) > 0)
+        return bcjr::kKernelB4;
+    return bcjr::kKernelGeneric;
 }
 
+size_t kernel_bytes(int kernel, int B, int N, int L, int b, int V, int mode, int sms) {
+    switch (kernel) {
+        case bcjr::kKernelL16: return bcjr::l16_workspace_bytes(B, N, mode);
+        case bcjr::kKernelB4: return bcjr::b4_workspace_bytes(B, N, mode);
+        default: return bcjr::generic_workspace_bytes(B, N, L, b, V, mode, sms);
+    }
+}
+
+// Workspace that bcjr_workspace_bytes reports: what the kernel chosen for an
+// aligned codebook needs, and at least one sequence slot of the generic
+// kernels (all they need), so that the same workspace serves a call whose
+// codebook pointer sends it to the generic kernels.
 size_t data_bytes(int B, int N, int L, int b, int V, int mode, int sms) {
-    if (use_l16(B, N, L, b, V, mode)) return bcjr::l16_workspace_bytes(B, N, mode);
-    return bcjr::generic_workspace_bytes(B, N, L, b, V, mode, sms);
+    const size_t k = kernel_bytes(pick_kernel(B, N, L, b, V, mode, nullptr), B, N, L, b, V, mode, sms);
+    const size_t g1 = bcjr::generic_workspace_bytes(1, N, L, b, V, mode, sms);
+    return k > g1 ? k : g1;
 }
 
 int prepare(bcjr::LaunchArgs &a, void *ws, size_t ws_bytes, int mode) {
@@ -81,18 +101,22 @@ int prepare(bcjr::LaunchArgs &a, void *ws, size_t ws_bytes, int mode) {
     if (st) return st;
     if (!ws) return BCJR_ERR_WORKSPACE;
     if (!aligned(ws, 256)) return BCJR_ERR_ALIGNMENT;
-    const size_t need = data_bytes(a.B, a.N, a.L, a.BB, a.V, mode, d.sms);
+    a.kernel = pick_kernel(a.B, a.N, a.L, a.BB, a.V, mode, a.cb);
+    // The cluster kernels need their full workspace; the generic kernels run
+    // as many sequence slots as the workspace holds (at least one).
+    const size_t need = a.kernel == bcjr::kKernelGeneric
+                            ? 0
+                            : kernel_bytes(a.kernel, a.B, a.N, a.L, a.BB, a.V, mode, d.sms);
     if (ws_bytes < kHeaderBytes + need) return BCJR_ERR_WORKSPACE;
     a.status = reinterpret_cast<int *>(ws);
     a.ws_data = static_cast<char *>(ws) + kHeaderBytes;
     a.ws_data_bytes = ws_bytes - kHeaderBytes;
     a.mode = mode;
-    a.fast = use_l16(a.B, a.N, a.L, a.BB, a.V, mode);
     // Test-only: BCJR_B200_TEST_DROP_SENDS=1 makes the cluster kernel's CTA 1
     // withhold its outputs so that the bounded waits time out (tests/ only).
     const char *drop = std::getenv("BCJR_B200_TEST_DROP_SENDS");
     a.drop_sends = (drop && drop[0] == '1') ? 1 : 0;
-    a.grid = a.fast ? 1 : bcjr::generic_grid(a.B, a.N, a.L, a.BB, mode, a.ws_data_bytes);
+    a.grid = a.kernel != bcjr::kKernelGeneric ? 1 : bcjr::generic_grid(a.B, a.N, a.L, a.BB, mode, a.ws_data_bytes);
     if (a.grid < 1) return BCJR_ERR_WORKSPACE;
     if (cudaMemsetAsync(a.status, 0, sizeof(int), a.stream) != cudaSuccess) return BCJR_ERR_LAUNCH;
     return BCJR_OK;
@@ -103,7 +127,11 @@ int finish(cudaError_t e) {
 }
 
 cudaError_t launch(const bcjr::LaunchArgs &a) {
-    return a.fast ? bcjr::launch_l16(a) : bcjr::launch_generic(a);
+    switch (a.kernel) {
+        case bcjr::kKernelL16: return bcjr::launch_l16(a);
+        case bcjr::kKernelB4: return bcjr::launch_b4(a);
+        default: return bcjr::launch_generic(a);
+    }
 }
 
 }  // namespace

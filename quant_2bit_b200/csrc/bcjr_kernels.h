@@ -7,6 +7,7 @@
 namespace bcjr {
 
 enum { kModeForward = 0, kModeBackward = 1, kModeInternals = 2 };
+enum { kKernelGeneric = 0, kKernelL16 = 1, kKernelB4 = 2 };
 
 struct LaunchArgs {
     const float *seq, *cb, *T_dev;
@@ -20,8 +21,8 @@ struct LaunchArgs {
     int *status;                  // device status word in the workspace header
     int mode;
     int grid;
-    bool fast;                    // cluster kernel (bcjr_l16.cu)
-    int drop_sends;               // test-only fault injection (cluster kernel)
+    int kernel;                   // kKernelGeneric / kKernelL16 / kKernelB4
+    int drop_sends;               // test-only fault injection (cluster kernels)
     cudaStream_t stream;
 };
 
@@ -35,5 +36,11 @@ bool l16_applicable(int B, int N, int L, int BB, int V);
 int l16_clusters(int B, int mode);
 size_t l16_workspace_bytes(int B, int N, int mode);
 cudaError_t launch_l16(const LaunchArgs &a);
+
+// Cluster path for L=16, k=2, V=2 (b = 4), 2 <= N <= 512 (bcjr_b4.cu).
+bool b4_applicable(int B, int N, int L, int BB, int V);
+int b4_clusters(int B, int mode);
+size_t b4_workspace_bytes(int B, int N, int mode);
+cudaError_t launch_b4(const LaunchArgs &a);
 
 }  // namespace bcjr

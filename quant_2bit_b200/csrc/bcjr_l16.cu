@@ -30,13 +30,14 @@
 // cluster (a perfect shuffle).  Producers push them straight into the
 // consumer CTA's shared memory with st.async ... mbarrier::complete_tx, into
 // a double-buffered ring; the consumer arms each buffer's mbarrier with the
-// expected byte count.  Every step reads all its inputs first, then passes
-// one __syncthreads, then computes and sends; a producer that has received
-// the complete input of consumption u therefore knows that every CTA has
-// finished reading consumption u-1, whose buffer it is about to overwrite.
-// Each CTA's minimum output cost travels with the data (sent by warp 0 after
-// the next barrier), so every consumer renormalises by the exact global
-// minimum of the previous step; shifts accumulate in double.
+// expected byte count.  There is no block barrier per step: each warp that
+// finishes a step folds its minimum output cost into a shared-memory minimum
+// and counts itself in; the last warp of the CTA sends the CTA minimum to
+// every consumer, as part of the same consumption's byte count.  A producer
+// that has received the complete input of consumption u therefore knows
+// that every warp of every CTA has finished reading consumption u-1, whose
+// buffer it is about to overwrite.  Every consumer renormalises by the exact
+// global minimum of the previous step; shifts accumulate in double.
 //
 // Two sequences ("slots") are interleaved step by step so that one slot's
 // exchange latency hides behind the other's arithmetic.  Alpha / H rows go
@@ -50,11 +51,13 @@
 // and runs to completion.  The recursions are documented in bcjr_common.cuh.
 #include <cstdint>
 
-#include "bcjr_common.cuh"
+#include "bcjr_cluster.cuh"
 #include "bcjr_kernels.h"
 
 namespace bcjr {
 namespace l16 {
+
+using namespace clu;
 
 constexpr int kL = 16;
 constexpr int kB = 2;                 // branch bits b = kV
@@ -67,7 +70,6 @@ constexpr int kJPT = kJPC / kNT;      // 2 butterflies per thread
 constexpr int kSlots = 2;             // sequences in flight per cluster
 constexpr int kNMax = 512;            // longest sequence staged in shared memory
 constexpr int kWarps = kNT / 32;
-constexpr float kPosInf = __builtin_huge_valf();
 
 template <bool GRAD>
 struct alignas(128) Smem {
@@ -88,147 +90,6 @@ struct alignas(128) Smem {
     int cnt[kSlots][2];                   // warps finished with the step
     int hiss[kSlots];                     // TMA row loads issued per slot
 };
-
-// ---------------------------------------------------------------------------
-// PTX wrappers.
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_id() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t num_clusters() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arm(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-// try_wait suspends the thread until the phase completes or ~20 us pass.
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;"
-        " selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(20000)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ void st_async4(uint32_t addr, float a, float b, float c, float d,
-                                          uint32_t bar) {
-    asm volatile(
-        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1,%2,%3,%4}, [%5];"
-        ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void st_async1(uint32_t addr, float a, uint32_t bar) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
-                 ::"r"(addr), "r"(__float_as_uint(a)), "r"(bar)
-                 : "memory");
-}
-__device__ __forceinline__ void st_cluster(uint32_t addr, float a) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(a) : "memory");
-}
-// One TMA bulk copy global -> own shared memory, completing on `bar`.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
-                                         uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Bounded wait: ~1 s, then BCJR_ERR_TIMEOUT in the status word.  Once any
-// thread of the grid has failed, every later wait returns at once.
-__device__ __forceinline__ void wait_bar(uint32_t bar, uint32_t parity, int *status,
-                                         bool &failed) {
-    if (failed) return;
-    if (mbar_try(bar, parity)) return;
-    const unsigned long long t0 = global_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try(bar, parity)) return;
-        if ((i & 7) == 0) {
-            if (*reinterpret_cast<volatile int *>(status) != 0) {
-                failed = true;
-                return;
-            }
-            if (global_ns() - t0 > 1000000000ull) {
-                atomicExch(status, 8 /* BCJR_ERR_TIMEOUT */);
-                failed = true;
-                return;
-            }
-        }
-    }
-}
-
-// f32x2 pairs (FADD2 / FMUL2 / FFMA2 through the sm_100 float2 builtins).
-using F2 = float2;
-__device__ __forceinline__ F2 mk(float a, float b) { return make_float2(a, b); }
-__device__ __forceinline__ F2 bc(float a) { return make_float2(a, a); }
-__device__ __forceinline__ F2 add2(F2 a, F2 b) { return __fadd2_rn(a, b); }
-__device__ __forceinline__ F2 sub2(F2 a, F2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }
-__device__ __forceinline__ F2 mul2(F2 a, F2 b) { return __fmul2_rn(a, b); }
-__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) { return __ffma2_rn(a, b, c); }
-__device__ __forceinline__ float min3(float a, float b, float c) {
-    float r;
-    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-    return r;
-}
-__device__ __forceinline__ float min4(float a, float b, float c, float d) {
-    return fminf(min3(a, b, c), d);
-}
-__device__ __forceinline__ F2 ex2p(F2 a) { return F2{ex2(a.x), ex2(a.y)}; }
-
-// Minimum over the warp (all 32 lanes active).
-__device__ __forceinline__ float redux_min(float v) {
-    float r;
-    asm volatile("redux.sync.min.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
-    return r;
-}
-
-// Order-preserving map float -> int (and back): a < b  <=>  key(a) < key(b).
-__device__ __forceinline__ int order_key(float f) {
-    const int i = __float_as_int(f);
-    return i >= 0 ? i : i ^ 0x7fffffff;
-}
-__device__ __forceinline__ float order_key_inv(int k) {
-    return __int_as_float(k >= 0 ? k : k ^ 0x7fffffff);
-}
-
-// Soft-min accumulator (m, s): value = m - lg2 s, s = sum 2^(m - x).
-__device__ __forceinline__ void smin_merge(float &m, float &s, float m2, float s2) {
-    if (m2 < m) {
-        s = s * ex2(m2 - m) + s2;
-        m = m2;
-    } else if (m2 < kPosInf) {
-        s = s + s2 * ex2(m - m2);
-    }
-}
 
 // Workspace of one (cluster, slot): float offsets.
 struct SlotLayout {

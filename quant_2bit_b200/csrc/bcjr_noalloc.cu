@@ -90,7 +90,7 @@ extern "C" BCJR_API int bcjr_fb_forward_noalloc(const float *seq, const float *c
     a.ws_data_bytes = kNoAllocScratchBytes;
     a.status = nullptr;
     a.mode = bcjr::kModeForward;
-    a.fast = false;
+    a.kernel = bcjr::kKernelGeneric;
     a.grid = slots;
     a.stream = reinterpret_cast<cudaStream_t>(stream);
     return bcjr::launch_generic(a) == cudaSuccess ? BCJR_OK : BCJR_ERR_LAUNCH;

@@ -17,11 +17,32 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "slow: long-running")
 
 
+def hyb_codebook(lut, Q=9, L=16):
+    """(2^L, 2) HYB codebook from a (2^Q, 2) LUT: Klimov-Shamir hash x*x + x
+    (mod 2^32), LUT row (x >> (15 - Q)) & (2^Q - 1), second component negated
+    when bit 15 of the hash is set (the reference's HYB code,
+    src/codes/ref.py:99-114, src/qat/ste.py:376-392)."""
+    s = np.arange(1 << L, dtype=np.uint64)
+    x = (s * s + s) & np.uint64(0xFFFFFFFF)
+    idx = ((x >> np.uint64(15 - Q)) & np.uint64((1 << Q) - 1)).astype(np.int64)
+    out = np.asarray(lut, dtype=np.float32)[idx].copy()
+    flip = (x & np.uint64(1 << 15)) != 0
+    out[flip, 1] = -out[flip, 1]
+    return out
+
+
 def load_golden(name):
-    """A fixture written by tests/golden/make_golden.py (reference outputs)."""
+    """A fixture written by tests/golden/make_golden.py (reference outputs).
+    Large codebooks live in shared files (l16_cb.npy, l16v2_cb.npy); a HYB
+    fixture carries its LUT, and the codebook is rebuilt from it and checked
+    against the reference decoder's rows stored with it."""
     d = dict(np.load(os.path.join(GOLDEN, name)))
-    if "cb" not in d:
-        d["cb"] = np.load(os.path.join(GOLDEN, "l16_cb.npy"))
+    if "cb" not in d and "lut" in d:
+        d["cb"] = hyb_codebook(d["lut"])
+        assert np.array_equal(d["cb"][d["cb_rows"]], d["cb_at_rows"])
+    elif "cb" not in d:
+        shared = "l16v2_cb.npy" if name.startswith("l16v2_") else "l16_cb.npy"
+        d["cb"] = np.load(os.path.join(GOLDEN, shared))
     for key in ("L", "k", "V"):
         d[key] = int(d[key])
     d["T"] = float(d["T"])

@@ -11,7 +11,7 @@ Input generation follows the benchmark configs: torch.Generator seeded with
 ``seed``; the codebook is drawn first, then the weights; Student-t weights use
 numpy.random.default_rng(seed).standard_t(3) / sqrt(3).
 
-    python tests/golden/make_golden.py --ref <reference root> [--only c1|small|l16|v2|rht]
+    python tests/golden/make_golden.py --ref <reference root> [--only c1|small|l16|v2|v2sweep|rht]
 """
 import argparse
 import math
@@ -104,6 +104,31 @@ def gen_v2(ref_fb):
     save("l16_v2.npz", cb=cb, w=w, grad=grad, T=np.float64(T), L=L, k=k, V=V, **out)
 
 
+def gen_v2sweep(ref_fb, ref_root):
+    # b = 4 cluster-kernel cases: L=16, k=2, V=2, N=128, two sequences each;
+    # Gaussian codebook (shared file) at three temperatures, Student-t weights,
+    # and a HYB codebook built by the reference's decoder from a random LUT.
+    from src.codes.ref import decode_hyb_batch
+    L, k, V, N, B = 16, 2, 2, 128, 2
+    g = torch.Generator().manual_seed(5)
+    cb = torch.randn(1 << L, V, generator=g).numpy()
+    np.save(os.path.join(HERE, "l16v2_cb.npy"), cb)
+    w = torch.randn(B, N, V, generator=g).numpy()
+    grad = torch.randn(B, N, V, generator=g).numpy()
+    for T in (0.05, 0.25, 2.0):
+        out = run_ref(ref_fb, w, cb, T, L, k, V, grad)
+        save(f"l16v2_gauss_T{T:g}.npz", w=w, grad=grad, T=np.float64(T), L=L, k=k, V=V, **out)
+    w3 = (np.random.default_rng(5).standard_t(3, size=(B, N, V)) / math.sqrt(3.0)).astype(np.float32)
+    out = run_ref(ref_fb, w3, cb, 0.5, L, k, V, grad)
+    save("l16v2_t3_T0.5.npz", w=w3, grad=grad, T=np.float64(0.5), L=L, k=k, V=V, **out)
+    lut = np.random.default_rng(6).standard_normal((512, 2)).astype(np.float32)
+    cb_hyb = decode_hyb_batch(np.arange(1 << L, dtype=np.uint32), lut, Q=9)
+    rows = np.random.default_rng(7).integers(0, 1 << L, size=256)
+    out = run_ref(ref_fb, w, cb_hyb, 0.3, L, k, V, grad)
+    save("l16v2_hyb_T0.3.npz", w=w, grad=grad, T=np.float64(0.3), L=L, k=k, V=V, lut=lut,
+         cb_rows=rows, cb_at_rows=cb_hyb[rows], **out)
+
+
 def gen_rht(ref_root):
     # RHT, sign vectors and tile order of the reference's quantizer wrapper
     # (src/rht/transform.py:59-126, src/qat/ste.py:76-110).
@@ -127,10 +152,12 @@ def main():
     sys.path.insert(0, args.ref)
     from src.bcjr.forward_backward import bcjr_forward_backward as ref_fb
     torch.set_num_threads(os.cpu_count() or 1)
-    todo = [args.only] if args.only else ["small", "c1", "v2", "l16", "rht"]
+    todo = [args.only] if args.only else ["small", "c1", "v2", "l16", "v2sweep", "rht"]
     for what in todo:
         if what == "rht":
             gen_rht(args.ref)
+        elif what == "v2sweep":
+            gen_v2sweep(ref_fb, args.ref)
         else:
             {"c1": gen_c1, "small": gen_small, "l16": gen_l16, "v2": gen_v2}[what](ref_fb)
 

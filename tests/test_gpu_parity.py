@@ -18,7 +18,7 @@ from oracle import oracle, torch_port
 pytestmark = pytest.mark.gpu
 
 ALL_GOLDEN = (golden_names("small_*.npz") + golden_names("c1_*.npz")
-              + golden_names("l16_*.npz"))
+              + golden_names("l16_*.npz") + golden_names("l16v2_*.npz"))
 
 
 def run_ours(w, cb, T, L, k, V, grad, T_as="cuda"):

@@ -5,11 +5,13 @@ Pins the checker before anything is checked against it: the C restatement
 reproduce the outputs of the reference itself (tests/golden/*.npz, made by
 importing the reference's eager bcjr_forward_backward).
 """
+import os
+
 import numpy as np
 import pytest
 import torch
 
-from conftest import golden_names, load_golden, parity_report
+from conftest import GOLDEN, golden_names, load_golden, parity_report
 from oracle import oracle, torch_port
 
 SMALL = golden_names("small_*.npz")
@@ -50,9 +52,11 @@ def test_c_oracle_config1(name):
     np.testing.assert_allclose(dseq, d["dseq64"], rtol=1e-8, atol=1e-10)
 
 
-@pytest.mark.parametrize("name", ["l16_gauss_T0.5.npz", "l16_t3_T0.05.npz", "l16_v2.npz"])
+@pytest.mark.parametrize("name", ["l16_gauss_T0.5.npz", "l16_t3_T0.05.npz", "l16_v2.npz",
+                                  "l16v2_gauss_T0.05.npz", "l16v2_hyb_T0.3.npz"])
 def test_c_oracle_l16(name):
-    """L=16 production trellis (V=1 at T=0.5 and the hardest T, and V=2)."""
+    """L=16 production trellis (V=1 at T=0.5 and the hardest T; V=2 at T=0.5,
+    at the hardest T, and with a HYB codebook)."""
     d = load_golden(name)
     soft, logZ, dseq = oracle.fb(d["w"], d["cb"], d["T"], d["L"], d["k"], d["V"],
                                  grad_soft=d["grad"], dtype=np.float64)
@@ -133,3 +137,16 @@ def test_reference_own_error_is_recorded():
     d = load_golden("l16_gauss_T0.05.npz")
     own = np.abs(d["soft32"] - d["soft64"]).max()
     assert own > 1e-5
+
+
+def test_hyb_codebook_matches_reference_decoder():
+    """The HYB codebook rebuilt from the fixture's LUT equals the reference
+    decoder's output (src/codes/ref.py:99-114) on the rows stored with it,
+    and has the code's structure: every row is +-a LUT row."""
+    from conftest import hyb_codebook
+    d = dict(np.load(os.path.join(GOLDEN, "l16v2_hyb_T0.3.npz")))
+    cb = hyb_codebook(d["lut"])
+    np.testing.assert_array_equal(cb[d["cb_rows"]], d["cb_at_rows"])
+    assert cb.shape == (65536, 2)
+    assert np.isin(cb[:, 0], d["lut"][:, 0]).all()
+    assert np.isin(np.abs(cb[:, 1]), np.abs(d["lut"][:, 1])).all()
