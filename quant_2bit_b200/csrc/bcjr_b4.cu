@@ -71,8 +71,12 @@ constexpr int kNR = kG >> kB;         // 256 butterflies
 constexpr int kCL = 4;                // CTAs per cluster
 constexpr int kRPC = kNR / kCL;       // 64 butterflies per CTA
 constexpr int kIn = kRPC * 16;        // 1024 inputs per CTA per step and plane
-constexpr int kNT = 512;              // threads per CTA
-constexpr int kWarps = kNT / 32;
+#ifndef BCJR_B4_VT
+#define BCJR_B4_VT 2
+#endif
+constexpr int kVT = BCJR_B4_VT;       // work units ("virtual threads") per thread
+constexpr int kNT = 512 / kVT;        // threads per CTA
+constexpr int kWarps = kNT / 32;      // warps per CTA
 #ifndef BCJR_B4_SLOTS
 #define BCJR_B4_SLOTS 2
 #endif
@@ -164,61 +168,75 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     const float two_over_T = 2.f / T;
     const float a0 = -(float)kB * ikap;     // cost of A_0 = b everywhere
 
-    // Alpha-sweep ownership: one c, butterflies rla and rla + 16 (local).
-    const int ac = lane & 15;
-    const int aq = 2 * warp + (lane >> 4);
-    const int arl = (aq & 15) + 32 * (aq >> 4);
-    // Alpha outputs: consumer CTA, and float offset in its alpha-ring plane.
-    const uint32_t a_dst = (uint32_t)((aq & 15) >> 2);
-    const uint32_t a_off = 2u * ((uint32_t)(2 * (int)rank + (aq >> 4)) * kRPC +
-                                 (uint32_t)(16 * (aq & 3) + ac));
-    // Beta-sweep ownership: p = warp, butterflies 2 lane and 2 lane + 1 (local).
-    const int bp = warp;
+    // Each thread carries kVT work units; unit h of thread (warp, lane) is
+    // virtual warp vw = warp + kWarps h, lane `lane` of a 512-unit layout.
+    // Alpha-sweep ownership of a unit: one c, butterflies rla and rla + 16 (local).
+    // Beta-sweep ownership: p = vw, butterflies 2 lane and 2 lane + 1 (local),
+    // the same butterflies for every unit of the thread.
+    int ac[kVT], arl[kVT], bp[kVT];
+    uint32_t a_off[kVT], a_base[kVT], b_off[kVT], b_base[kVT];
     const int brl = 2 * lane;
-    const uint32_t b_dst = (uint32_t)(bp >> 2);
-    const uint32_t b_off = beta_off((uint32_t)(16 * (bp & 3) + 4 * (int)rank + (lane >> 3)),
-                                    (uint32_t)(2 * (lane & 7)));
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem_raw);
+#pragma unroll
+    for (int h = 0; h < kVT; ++h) {
+        const int vw = warp + kWarps * h;
+        ac[h] = lane & 15;
+        const int aq = 2 * vw + (lane >> 4);
+        arl[h] = (aq & 15) + 32 * (aq >> 4);
+        // alpha outputs: consumer CTA, and float offset in its alpha-ring plane
+        a_base[h] = mapa(sbase, (uint32_t)((aq & 15) >> 2));
+        a_off[h] = 2u * ((uint32_t)(2 * (int)rank + (aq >> 4)) * kRPC + (uint32_t)(16 * (aq & 3) + ac[h]));
+        bp[h] = vw;
+        b_base[h] = mapa(sbase, (uint32_t)(vw >> 2));
+        b_off[h] = beta_off((uint32_t)(16 * (vw & 3) + 4 * (int)rank + (lane >> 3)),
+                            (uint32_t)(2 * (lane & 7)));
+    }
+    // history-row chunk (global) of my alpha outputs: consumer CTA index
+    uint32_t a_dst[kVT];
+#pragma unroll
+    for (int h = 0; h < kVT; ++h) {
+        const int aq = 2 * (warp + kWarps * h) + (lane >> 4);
+        a_dst[h] = (uint32_t)((aq & 15) >> 2);
+    }
 
-    // Codebook of the current sweep's 32 states, f32x2 pairs along the
-    // reduced index: C0 = first component, C1 = second.
-    F2 C0[2][8], C1[2][8];
+    // Codebook of the current sweep's 32 states per unit, f32x2 pairs along
+    // the reduced index: C0 = first component, C1 = second.
+    F2 C0[kVT][2][8], C1[kVT][2][8];
     const float2 *cb2 = reinterpret_cast<const float2 *>(cb);
     auto load_alpha_cb = [&]() {
 #pragma unroll
+        for (int h = 0; h < kVT; ++h)
+#pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
-            const int r = (int)rank * kRPC + arl + 16 * rr;
+            const int r = (int)rank * kRPC + arl[h] + 16 * rr;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float2 u = __ldg(cb2 + (2 * i) * kG + 16 * r + ac);
-                const float2 v = __ldg(cb2 + (2 * i + 1) * kG + 16 * r + ac);
-                C0[rr][i] = mk(u.x, v.x);
-                C1[rr][i] = mk(u.y, v.y);
+                const float2 u = __ldg(cb2 + (2 * i) * kG + 16 * r + ac[h]);
+                const float2 v = __ldg(cb2 + (2 * i + 1) * kG + 16 * r + ac[h]);
+                C0[h][rr][i] = mk(u.x, v.x);
+                C1[h][rr][i] = mk(u.y, v.y);
             }
         }
     };
     auto load_beta_cb = [&]() {
 #pragma unroll
+        for (int h = 0; h < kVT; ++h)
+#pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
             const int r = (int)rank * kRPC + brl + rr;
-            const float4 *base = reinterpret_cast<const float4 *>(cb2 + bp * kG + 16 * r);
+            const float4 *base = reinterpret_cast<const float4 *>(cb2 + bp[h] * kG + 16 * r);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const float4 v = __ldg(base + i);
-                C0[rr][i] = mk(v.x, v.z);
-                C1[rr][i] = mk(v.y, v.w);
+                C0[h][rr][i] = mk(v.x, v.z);
+                C1[h][rr][i] = mk(v.y, v.w);
             }
         }
     };
 
-    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem_raw);
-    uint32_t cbase[kCL];
-#pragma unroll
-    for (int r = 0; r < kCL; ++r) cbase[r] = mapa(sbase, r);
     auto soff = [&](const void *p) -> uint32_t {
         return (uint32_t)__cvta_generic_to_shared(p) - sbase;
     };
-    const uint32_t a_base = mapa(sbase, a_dst);   // consumer CTA of my alpha outputs
-    const uint32_t b_base = mapa(sbase, b_dst);   // consumer CTA of my beta outputs
 
     for (int i = tid; i < kPlanes * kIn; i += kNT) (&sm.zero[0][0])[i] = 0.f;
     if (tid == 0) {
@@ -363,15 +381,18 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 const bool last = (t == N - 1);
                 const F2 W0 = bc(wv.x), W1 = bc(wv.y), G0 = bc(gv.x), G1 = bc(gv.y),
                          GS = bc(gs), NK = bc(-kap);
-                float o[2], hh[2];
+                float o[kVT][2], hh[kVT][2];
+                float lmin = kPosInf;
+#pragma unroll
+                for (int h = 0; h < kVT; ++h) {
 #pragma unroll
                 for (int rr = 0; rr < 2; ++rr) {
-                    const int rl = arl + 16 * rr;
+                    const int rl = arl[h] + 16 * rr;
                     F2 x[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const F2 A = *reinterpret_cast<const F2 *>(in + 2 * (i * kRPC + rl));
-                        const F2 d0 = sub2(C0[rr][i], W0), d1 = sub2(C1[rr][i], W1);
+                        const F2 d0 = sub2(C0[h][rr][i], W0), d1 = sub2(C1[h][rr][i], W1);
                         x[i] = fma2(d1, d1, fma2(d0, d0, A));
                     }
                     const float m = min16(x);
@@ -381,35 +402,37 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     for (int i = 0; i < 8; ++i) e[i] = ex2p(fma2(x[i], NK, KM));
                     const F2 S2 = sum8(e);
                     const float S = S2.x + S2.y;
-                    o[rr] = fmaf(-lg2(S), ikap, m - sub);
+                    o[h][rr] = fmaf(-lg2(S), ikap, m - sub);
                     if (GRAD) {
                         F2 hf = bc(0.f);
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
                             const F2 H = *reinterpret_cast<const F2 *>(in + kIn + 2 * (i * kRPC + rl));
-                            const F2 f = fma2(C0[rr][i], G0, fma2(C1[rr][i], G1, sub2(H, GS)));
+                            const F2 f = fma2(C0[h][rr][i], G0, fma2(C1[h][rr][i], G1, sub2(H, GS)));
                             hf = fma2(e[i], f, hf);
                         }
-                        hh[rr] = (hf.x + hf.y) * rcp(S);
+                        hh[h][rr] = (hf.x + hf.y) * rcp(S);
                     }
                 }
+                lmin = min3(lmin, o[h][0], o[h][1]);
                 if (!last) {
                     if (!failed && !drop) {
-                        const uint32_t bar = a_base + soff(&sm.full[z][nb]);
-                        const uint32_t o0 = a_base + soff(&sm.buf[z][nb][0][0]) + 4u * a_off;
-                        st_async2(o0, o[0], o[1], bar);
-                        if (GRAD) st_async2(o0 + kIn * 4, hh[0], hh[1], bar);
+                        const uint32_t bar = a_base[h] + soff(&sm.full[z][nb]);
+                        const uint32_t o0 = a_base[h] + soff(&sm.buf[z][nb][0][0]) + 4u * a_off[h];
+                        st_async2(o0, o[h][0], o[h][1], bar);
+                        if (GRAD) st_async2(o0 + kIn * 4, hh[h][0], hh[h][1], bar);
                     }
                     // history row t + 1, in the consumer's chunk
                     float *hrow = slot_ws[z] + lay.hist + (long)(t + 1) * kRowFloats +
-                                  a_dst * (kPlanes * kIn) + a_off;
-                    *reinterpret_cast<float2 *>(hrow) = make_float2(o[0], o[1]);
-                    if (GRAD) *reinterpret_cast<float2 *>(hrow + kIn) = make_float2(hh[0], hh[1]);
+                                  a_dst[h] * (kPlanes * kIn) + a_off[h];
+                    *reinterpret_cast<float2 *>(hrow) = make_float2(o[h][0], o[h][1]);
+                    if (GRAD) *reinterpret_cast<float2 *>(hrow + kIn) = make_float2(hh[h][0], hh[h][1]);
                 } else {
-                    smin_merge(lzm[z], lzs[z], kap * o[0], 1.f);
-                    smin_merge(lzm[z], lzs[z], kap * o[1], 1.f);
+                    smin_merge(lzm[z], lzs[z], kap * o[h][0], 1.f);
+                    smin_merge(lzm[z], lzs[z], kap * o[h][1], 1.f);
                 }
-                finish_step(z, nb, !last && !drop, fminf(o[0], o[1]), nullptr, bc(0.f), 0,
+                }
+                finish_step(z, nb, !last && !drop, lmin, nullptr, bc(0.f), 0,
                             slot_ws);
             }
         }
@@ -437,8 +460,8 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 for (int i = 0; i < kWarps; ++i) smin_merge(m, s, sm.wmin[z][i], sm.wacc[z][i]);
 #pragma unroll
                 for (int r = 0; r < kCL; ++r) {
-                    st_cluster(cbase[r] + soff(&sm.lz[z][rank][0]), m);
-                    st_cluster(cbase[r] + soff(&sm.lz[z][rank][1]), s);
+                    st_cluster(mapa(sbase, (uint32_t)r) + soff(&sm.lz[z][rank][0]), m);
+                    st_cluster(mapa(sbase, (uint32_t)r) + soff(&sm.lz[z][rank][1]), s);
                 }
             }
         }
@@ -487,18 +510,23 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     ++use[z];
                 }
                 U[z] += (double)sigma;
-                float ah[2] = {a0, a0}, hp[2] = {0.f, 0.f};
+                float ah[kVT][2], hp[kVT][2];
+#pragma unroll
+                for (int h = 0; h < kVT; ++h) { ah[h][0] = ah[h][1] = a0; hp[h][0] = hp[h][1] = 0.f; }
                 if (tn > 0) {
                     wait_bar(sbase + soff(&sm.hbar[z]), hcnt[z] & 1, status, failed);
                     ++hcnt[z];
-                    const int o4 = 2 * ((bp >> 1) * kRPC + brl);
-                    const float4 va = *reinterpret_cast<const float4 *>(&sm.hst[z][0][o4]);
-                    ah[0] = (bp & 1) ? va.y : va.x;
-                    ah[1] = (bp & 1) ? va.w : va.z;
-                    if (GRAD) {
-                        const float4 vh = *reinterpret_cast<const float4 *>(&sm.hst[z][kPlanes - 1][o4]);
-                        hp[0] = (bp & 1) ? vh.y : vh.x;
-                        hp[1] = (bp & 1) ? vh.w : vh.z;
+#pragma unroll
+                    for (int h = 0; h < kVT; ++h) {
+                        const int o4 = 2 * ((bp[h] >> 1) * kRPC + brl);
+                        const float4 va = *reinterpret_cast<const float4 *>(&sm.hst[z][0][o4]);
+                        ah[h][0] = (bp[h] & 1) ? va.y : va.x;
+                        ah[h][1] = (bp[h] & 1) ? va.w : va.z;
+                        if (GRAD) {
+                            const float4 vh = *reinterpret_cast<const float4 *>(&sm.hst[z][kPlanes - 1][o4]);
+                            hp[h][0] = (bp[h] & 1) ? vh.y : vh.x;
+                            hp[h][1] = (bp[h] & 1) ? vh.w : vh.z;
+                        }
                     }
                 }
                 const double Oa = tn > 0 ? sm.offs[z][tn - 1] : 0.0;
@@ -515,26 +543,34 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 const F2 W0 = bc(wv.x), W1 = bc(wv.y), G0 = bc(gv.x), G1 = bc(gv.y),
                          GS = bc(gs), NK = bc(-kap);
                 F2 acc = bc(0.f);
-                float ob[2] = {0.f, 0.f}, bbo[2] = {0.f, 0.f};
+                float ob[kVT][2], bbo[kVT][2];
 #pragma unroll
                 for (int rr = 0; rr < 2; ++rr) {
-                    // this lane's 128-byte region: butterflies 2 lane, 2 lane + 1
+                    // this lane's 128-byte region: butterflies 2 lane, 2 lane + 1,
+                    // the inputs of every unit of the thread
                     auto chunk = [&](int plane, int q) -> float4 {
                         const uint32_t off = (uint32_t)lane * 32u +
                                              ((uint32_t)((rr << 2) | q) ^ ((uint32_t)lane & 7u)) * 4u;
                         return *reinterpret_cast<const float4 *>(in + plane * kIn + off);
                     };
-                    F2 bin[8];
+                    F2 bin[8], bbin[8];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const float4 v = chunk(0, q);
                         bin[2 * q] = mk(v.x, v.y);
                         bin[2 * q + 1] = mk(v.z, v.w);
+                        if (GRAD) {
+                            const float4 u = chunk(kPlanes - 1, q);
+                            bbin[2 * q] = sub2(mk(u.x, u.y), GS);
+                            bbin[2 * q + 1] = sub2(mk(u.z, u.w), GS);
+                        }
                     }
+#pragma unroll
+                    for (int h = 0; h < kVT; ++h) {
                     F2 x[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const F2 d0 = sub2(C0[rr][i], W0), d1 = sub2(C1[rr][i], W1);
+                        const F2 d0 = sub2(C0[h][rr][i], W0), d1 = sub2(C1[h][rr][i], W1);
                         x[i] = fma2(d1, d1, fma2(d0, d0, bin[i]));
                     }
                     const float m = min16(x);
@@ -545,44 +581,49 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     const F2 S2 = sum8(e);
                     const float S = S2.x + S2.y;
                     const float ms = m - sigma;
-                    if (t >= 0) ob[rr] = fmaf(-lg2(S), ikap, ms);
-                    const float f = ex2(fmaf(ms + ah[rr], -kap, Cb));
+                    ob[h][rr] = t >= 0 ? fmaf(-lg2(S), ikap, ms) : 0.f;
+                    const float f = ex2(fmaf(ms + ah[h][rr], -kap, Cb));
                     if (!GRAD) {
-                        F2 e0 = mul2(e[0], C0[rr][0]), e1 = mul2(e[0], C1[rr][0]);
+                        F2 e0 = mul2(e[0], C0[h][rr][0]), e1 = mul2(e[0], C1[h][rr][0]);
 #pragma unroll
                         for (int i = 1; i < 8; ++i) {
-                            e0 = fma2(e[i], C0[rr][i], e0);
-                            e1 = fma2(e[i], C1[rr][i], e1);
+                            e0 = fma2(e[i], C0[h][rr][i], e0);
+                            e1 = fma2(e[i], C1[h][rr][i], e1);
                         }
                         acc = fma2(bc(f), mk(e0.x + e0.y, e1.x + e1.y), acc);
+                        bbo[h][rr] = 0.f;
                     } else {
-                        const F2 HP = bc(hp[rr]);
+                        const F2 HP = bc(hp[h][rr]);
                         F2 ey = bc(0.f), sv = bc(0.f), s0 = bc(0.f), s1 = bc(0.f);
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            const float4 u = chunk(kPlanes - 1, i >> 1);
-                            const F2 bb = (i & 1) ? mk(u.z, u.w) : mk(u.x, u.y);
-                            const F2 y = fma2(C0[rr][i], G0, fma2(C1[rr][i], G1, sub2(bb, GS)));
+                            const F2 y = fma2(C0[h][rr][i], G0, fma2(C1[h][rr][i], G1, bbin[i]));
                             ey = fma2(e[i], y, ey);
                             const F2 v = mul2(e[i], add2(y, HP));
                             sv = add2(sv, v);
-                            s0 = fma2(v, C0[rr][i], s0);
-                            s1 = fma2(v, C1[rr][i], s1);
+                            s0 = fma2(v, C0[h][rr][i], s0);
+                            s1 = fma2(v, C1[h][rr][i], s1);
                         }
-                        bbo[rr] = (ey.x + ey.y) * rcp(S);
+                        bbo[h][rr] = (ey.x + ey.y) * rcp(S);
                         const float SV = sv.x + sv.y;
                         acc = fma2(bc(f), mk(fmaf(-st.x, SV, s0.x + s0.y), fmaf(-st.y, SV, s1.x + s1.y)),
                                    acc);
                     }
+                    }
                 }
-                if (t >= 0 && !failed) {
-                    const uint32_t bar = b_base + soff(&sm.full[z][nb]);
-                    const uint32_t o0 = b_base + soff(&sm.buf[z][nb][0][0]) + 4u * b_off;
-                    st_async2(o0, ob[0], ob[1], bar);
-                    if (GRAD) st_async2(o0 + kIn * 4, bbo[0], bbo[1], bar);
+                float lmin = kPosInf;
+#pragma unroll
+                for (int h = 0; h < kVT; ++h) {
+                    lmin = min3(lmin, ob[h][0], ob[h][1]);
+                    if (t >= 0 && !failed) {
+                        const uint32_t bar = b_base[h] + soff(&sm.full[z][nb]);
+                        const uint32_t o0 = b_base[h] + soff(&sm.buf[z][nb][0][0]) + 4u * b_off[h];
+                        st_async2(o0, ob[h][0], ob[h][1], bar);
+                        if (GRAD) st_async2(o0 + kIn * 4, bbo[h][0], bbo[h][1], bar);
+                    }
                 }
                 float *part_row = slot_ws[z] + lay.part + ((long)tn * kCL + rank) * kWarps * 2;
-                finish_step(z, nb, t >= 0, fminf(ob[0], ob[1]), part_row, acc, tn - 1, slot_ws);
+                finish_step(z, nb, t >= 0, lmin, part_row, acc, tn - 1, slot_ws);
             }
         }
         __syncthreads();

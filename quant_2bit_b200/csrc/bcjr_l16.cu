@@ -1,5 +1,8 @@
 // Production kernel for the QTIP trellis L=16, k=2, V=1 (b = 2): one
-// 4-CTA thread-block cluster per pair of sequences, one CTA per SM.
+// 2-CTA thread-block cluster per pair of sequences (forward) or per sequence
+// (backward), one CTA per SM.  Clusters of 2 tile all 148 SMs of a B200
+// (74 clusters); clusters of 4 fit only 33 (132 SMs), and measured 14 %
+// slower (BCJR_L16_CL=4 still builds that variant).
 //
 // Work decomposition
 // ------------------
@@ -8,10 +11,10 @@
 // In the forward (alpha) direction butterfly j reads the four group values
 // A_t(p 2^12 + j) and writes A_{t+1}(4 j + c); in the backward (beta)
 // direction it reads Bt_{t+1}(4 j + c) and writes Bt_t(p 2^12 + j).  Every
-// step touches the same 16 states per butterfly, so each thread owns two
-// butterflies for the whole kernel and keeps their 32 codebook values in
-// registers: no codebook traffic after the first load.  CTA r of the cluster
-// owns butterflies [1024 r, 1024 r + 1024).
+// step touches the same 16 states per butterfly, so each thread owns
+// kJPT = 4 butterflies for the whole kernel and keeps their 64 codebook
+// values in registers: no codebook traffic after the first load.  CTA r of
+// the cluster owns butterflies [2048 r, 2048 r + 2048).
 //
 // Arithmetic
 // ----------
@@ -40,7 +43,8 @@
 // global minimum of the previous step; shifts accumulate in double.
 //
 // Two sequences ("slots") are interleaved step by step so that one slot's
-// exchange latency hides behind the other's arithmetic.  Alpha / H rows go
+// exchange latency hides behind the other's arithmetic (one in the 2-CTA
+// backward: its two 32 KB planes per ring buffer fill shared memory).  Alpha / H rows go
 // to a global history with float4 stores; the backward-time sweep fetches
 // the rows it needs one step ahead with TMA bulk copies (cp.async.bulk) into
 // shared memory.  Per-step partial sums of soft / d_seq are written per CTA
@@ -63,19 +67,31 @@ constexpr int kL = 16;
 constexpr int kB = 2;                 // branch bits b = kV
 constexpr int kG = 1 << (kL - kB);    // 16384 groups
 constexpr int kNJ = kG >> kB;         // 4096 butterflies
-constexpr int kCL = 4;                // CTAs per cluster
-constexpr int kJPC = kNJ / kCL;       // 1024 butterflies per CTA
+#ifndef BCJR_L16_CL
+#define BCJR_L16_CL 2
+#endif
+constexpr int kCL = BCJR_L16_CL;      // CTAs per cluster (4 or 2)
+constexpr int kJPC = kNJ / kCL;       // butterflies per CTA
+constexpr int kIn = 4 * kJPC;         // inputs per CTA per step and plane
 constexpr int kNT = 512;              // threads per CTA
-constexpr int kJPT = kJPC / kNT;      // 2 butterflies per thread
-constexpr int kSlots = 2;             // sequences in flight per cluster
+constexpr int kJPT = kJPC / kNT;      // butterflies per thread
+static_assert(kCL == 2 || kCL == 4, "cluster of 2 or 4 CTAs");
+// Sequences in flight per cluster, interleaved step by step: two, except in
+// the 2-CTA backward, whose two 32 KB planes per ring buffer leave shared
+// memory for one.
+template <bool GRAD>
+struct SlotsOf {
+    static constexpr int value = (kCL == 2 && GRAD) ? 1 : 2;
+};
 constexpr int kNMax = 512;            // longest sequence staged in shared memory
 constexpr int kWarps = kNT / 32;
 
 template <bool GRAD>
 struct alignas(128) Smem {
     static constexpr int kPlanes = GRAD ? 2 : 1;
-    float buf[kSlots][2][kPlanes][kNJ];   // input ring (16 KB per plane)
-    float hst[kSlots][kPlanes][kNJ];      // history rows staged by TMA: [p * 1024 + jl]
+    static constexpr int kSlots = SlotsOf<GRAD>::value;
+    float buf[kSlots][2][kPlanes][kIn];   // input ring (kIn floats per plane)
+    float hst[kSlots][kPlanes][kIn];      // history rows staged by TMA: [p * kJPC + jl]
     double offs[kSlots][kNMax];           // alpha shifts O_t
     float maxslot[kSlots][2][kCL];        // per-CTA minimum cost riding with the data
     float w[kSlots][kNMax];
@@ -90,6 +106,16 @@ struct alignas(128) Smem {
     int cnt[kSlots][2];                   // warps finished with the step
     int hiss[kSlots];                     // TMA row loads issued per slot
 };
+
+// Minimum of the kCL per-CTA minima riding with a consumption.
+__device__ __forceinline__ float cluster_min(const float *m) {
+    if (kCL == 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(m);
+        return min4(v.x, v.y, v.z, v.w);
+    }
+    const float2 v = *reinterpret_cast<const float2 *>(m);
+    return fminf(v.x, v.y);
+}
 
 // Workspace of one (cluster, slot): float offsets.
 struct SlotLayout {
@@ -120,7 +146,8 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     using SM = Smem<GRAD>;
     SM &sm = *reinterpret_cast<SM *>(smem_raw);
     constexpr int kPlanes = SM::kPlanes;
-    constexpr uint32_t kBytes = kPlanes * kNJ * 4 + kCL * 4;   // per consumption
+    constexpr int kSlots = SM::kSlots;
+    constexpr uint32_t kBytes = kPlanes * kIn * 4 + kCL * 4;   // per consumption
     constexpr uint32_t kRowBytes = kJPC * 4;                    // one TMA chunk
 
     const int tid = threadIdx.x;
@@ -136,7 +163,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     const float two_over_T = 2.f / T;
     const float a0 = -(float)kB * ikap;     // cost of A_0 = b everywhere
 
-    // Codebook of my two butterflies:
+    // Codebook of my kJPT butterflies:
     // cq[jj][c][h] = (c(2h, c), c(2h+1, c)),  c(p, c) = cb[p 2^14 + 4 j + c].
     int jg[kJPT];
     F2 cq[kJPT][4][2];
@@ -168,12 +195,13 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     uint32_t rdst[kJPT], aoff[kJPT];
 #pragma unroll
     for (int jj = 0; jj < kJPT; ++jj) {
+        // output A(4 j + c) is input p' = j >> 10 of butterfly (4 j + c) mod 4096
         const int j = jg[jj];
         rdst[jj] = cbase[0];
-        const uint32_t d = (uint32_t)(j >> 8) & 3u;
+        const uint32_t d = (uint32_t)(j & 1023) / (uint32_t)(kJPC / 4);
 #pragma unroll
         for (int r = 1; r < kCL; ++r) rdst[jj] = (d == (uint32_t)r) ? cbase[r] : rdst[jj];
-        aoff[jj] = 4u * (rank * kJPC + 4 * (j & 255));
+        aoff[jj] = 4u * (uint32_t)((j >> 10) * kJPC + 4 * (j & (kJPC / 4 - 1)));
     }
 
     if (tid == 0) {
@@ -196,13 +224,14 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     // Test-only fault injection (BCJR_B200_TEST_DROP_SENDS): CTA rank 1 never
     // sends its alpha-sweep outputs, so every consumer's bounded wait expires.
     const bool drop = drop_sends != 0 && rank == 1;
-    uint32_t use[kSlots] = {0, 0};    // ring consumptions per slot (uniform over the CTA)
-    uint32_t hcnt[kSlots] = {0, 0};   // TMA row loads waited per slot
+    uint32_t use[kSlots], hcnt[kSlots];   // ring consumptions / TMA row loads waited, per slot
+#pragma unroll
+    for (int z = 0; z < kSlots; ++z) use[z] = hcnt[z] = 0;
 
     // End of a step, per warp (no block barrier): the warp's minimum output
     // cost goes into the step's shared-memory minimum, its partial sum into
     // global memory, and the last warp to arrive sends the CTA minimum to the
-    // four consumers and, in the beta sweep, issues the next TMA rows (every
+    // kCL consumers and, in the beta sweep, issues the next TMA rows (every
     // warp of the CTA has read this step's inputs by then).
     // TMA rows of step tn (alpha costs, and H for the backward) into the
     // staging buffer of slot z; completion on hbar[z].
@@ -210,7 +239,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         const uint32_t hb = sbase + soff(&sm.hbar[z]);
         if (failed) return;
         atomicAdd(&sm.hiss[z], 1);
-        mbar_arm(hb, kPlanes * kNJ * 4);
+        mbar_arm(hb, kPlanes * kIn * 4);
         const float *hist = slot_ws[z] + lay.hist + (long)tn * kG + rank * kJPC;
 #pragma unroll
         for (int p = 0; p < 4; ++p)
@@ -280,37 +309,26 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         __syncthreads();
 
         // ------------------------------------------------------------ alpha
-        double O[kSlots] = {0.0, 0.0};
-        float lzm[kSlots] = {kPosInf, kPosInf}, lzs[kSlots] = {0.f, 0.f};
+        double O[kSlots];
+        float lzm[kSlots], lzs[kSlots];
+#pragma unroll
+        for (int z = 0; z < kSlots; ++z) { O[z] = 0.0; lzm[z] = kPosInf; lzs[z] = 0.f; }
         for (int t = 0; t < N; ++t) {
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
                 // inputs: costs of A_t minus the global minimum, and H_t
                 float shift;
-                float ain[kJPT][4], hin[kJPT][4];
+                const float *in = nullptr;   // this step's inputs (none at t = 0: all a_0)
                 if (t == 0) {
                     shift = a0;                    // a_0 is the same for every group
-#pragma unroll
-                    for (int jj = 0; jj < kJPT; ++jj)
-#pragma unroll
-                        for (int p = 0; p < 4; ++p) { ain[jj][p] = 0.f; hin[jj][p] = 0.f; }
                 } else {
                     const int x = use[z] & 1;
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
                     wait_bar(bar, (use[z] >> 1) & 1, status, failed);
-                    const float4 mx = *reinterpret_cast<const float4 *>(sm.maxslot[z][x]);
-                    shift = min4(mx.x, mx.y, mx.z, mx.w);
-#pragma unroll
-                    for (int jj = 0; jj < kJPT; ++jj) {
-                        const int jl = tid + kNT * jj;
-#pragma unroll
-                        for (int p = 0; p < 4; ++p) {
-                            ain[jj][p] = sm.buf[z][x][0][p * kJPC + jl] - shift;
-                            hin[jj][p] = GRAD ? sm.buf[z][x][kPlanes - 1][p * kJPC + jl] : 0.f;
-                        }
-                    }
+                    shift = cluster_min(sm.maxslot[z][x]);
+                    in = &sm.buf[z][x][0][0];
                     ++use[z];
                 }
                 O[z] += (double)shift;
@@ -331,8 +349,18 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 float *hhist = slot_ws[z] + lay.hhist + (long)(t + 1) * kG;
 #pragma unroll
                 for (int jj = 0; jj < kJPT; ++jj) {
-                    const F2 A01 = mk(ain[jj][0], ain[jj][1]), A23 = mk(ain[jj][2], ain[jj][3]);
-                    const F2 H01 = mk(hin[jj][0], hin[jj][1]), H23 = mk(hin[jj][2], hin[jj][3]);
+                    // costs of A_t minus the global minimum, and H_t, of my butterfly
+                    float ain[4] = {0.f, 0.f, 0.f, 0.f}, hin[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (in) {
+                        const int jl = tid + kNT * jj;
+#pragma unroll
+                        for (int p = 0; p < 4; ++p) {
+                            ain[p] = in[p * kJPC + jl] - shift;
+                            if (GRAD) hin[p] = in[kIn + p * kJPC + jl];
+                        }
+                    }
+                    const F2 A01 = mk(ain[0], ain[1]), A23 = mk(ain[2], ain[3]);
+                    const F2 H01 = mk(hin[0], hin[1]), H23 = mk(hin[2], hin[3]);
                     float o4[4], h4[4];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
@@ -359,7 +387,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                         if (!failed && !drop) {
                             st_async4(o0, o4[0], o4[1], o4[2], o4[3], bar);
                             if (GRAD)
-                                st_async4(o0 + kNJ * 4, h4[0], h4[1], h4[2], h4[3], bar);
+                                st_async4(o0 + kIn * 4, h4[0], h4[1], h4[2], h4[3], bar);
                         }
                         *reinterpret_cast<float4 *>(hist + 4 * j) = make_float4(o4[0], o4[1], o4[2], o4[3]);
                         if (GRAD)
@@ -403,7 +431,9 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         }
         cluster_sync();   // also publishes every CTA's history rows
 
-        double logZ2[kSlots] = {0.0, 0.0};
+        double logZ2[kSlots];
+#pragma unroll
+        for (int z = 0; z < kSlots; ++z) logZ2[z] = 0.0;
 #pragma unroll
         for (int z = 0; z < kSlots; ++z) {
             if (!active[z]) continue;
@@ -422,7 +452,9 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         }
 
         // ------------------------------------------------------------- beta
-        double U[kSlots] = {0.0, 0.0};
+        double U[kSlots];
+#pragma unroll
+        for (int z = 0; z < kSlots; ++z) U[z] = 0.0;
         for (int t = N - 2; t >= -1; --t) {
             const int tn = t + 1;
 #pragma unroll
@@ -430,56 +462,22 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 if (!active[z]) continue;
                 // inputs: costs of Bt_{t+1} minus the global minimum, Bb_{t+1},
                 // and this step's alpha / H rows
-                float sigma;
-                float bin[kJPT][4], bbin[kJPT][4];
-                if (t == N - 2) {
-                    sigma = 0.f;
-#pragma unroll
-                    for (int jj = 0; jj < kJPT; ++jj)
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) { bin[jj][c] = 0.f; bbin[jj][c] = 0.f; }
-                } else {
+                float sigma = 0.f;
+                const float *in = nullptr;   // Bt_{t+1}, Bb_{t+1} (none at t = N-2: all zero)
+                if (t != N - 2) {
                     const int x = use[z] & 1;
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
                     wait_bar(bar, (use[z] >> 1) & 1, status, failed);
-                    const float4 mx = *reinterpret_cast<const float4 *>(sm.maxslot[z][x]);
-                    sigma = min4(mx.x, mx.y, mx.z, mx.w);
-#pragma unroll
-                    for (int jj = 0; jj < kJPT; ++jj) {
-                        const int jl = tid + kNT * jj;
-                        const float4 v = *reinterpret_cast<const float4 *>(&sm.buf[z][x][0][4 * jl]);
-                        bin[jj][0] = v.x - sigma; bin[jj][1] = v.y - sigma;
-                        bin[jj][2] = v.z - sigma; bin[jj][3] = v.w - sigma;
-                        if (GRAD) {
-                            const float4 u = *reinterpret_cast<const float4 *>(&sm.buf[z][x][kPlanes - 1][4 * jl]);
-                            bbin[jj][0] = u.x; bbin[jj][1] = u.y; bbin[jj][2] = u.z; bbin[jj][3] = u.w;
-                        } else {
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) bbin[jj][c] = 0.f;
-                        }
-                    }
+                    sigma = cluster_min(sm.maxslot[z][x]);
+                    in = &sm.buf[z][x][0][0];
                     ++use[z];
                 }
                 U[z] += (double)sigma;
-                float a4[kJPT][4], h4[kJPT][4];
-                if (tn > 0) {
+                const bool hrow = tn > 0;    // this step's alpha / H rows are staged
+                if (hrow) {
                     wait_bar(sbase + soff(&sm.hbar[z]), hcnt[z] & 1, status, failed);
                     ++hcnt[z];
-#pragma unroll
-                    for (int jj = 0; jj < kJPT; ++jj) {
-                        const int jl = tid + kNT * jj;
-#pragma unroll
-                        for (int p = 0; p < 4; ++p) {
-                            a4[jj][p] = sm.hst[z][0][p * kJPC + jl];
-                            h4[jj][p] = GRAD ? sm.hst[z][kPlanes - 1][p * kJPC + jl] : 0.f;
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int jj = 0; jj < kJPT; ++jj)
-#pragma unroll
-                        for (int p = 0; p < 4; ++p) { a4[jj][p] = a0; h4[jj][p] = 0.f; }
                 }
                 const double Oa = tn > 0 ? sm.offs[z][tn - 1] : 0.0;
                 const float Cb = (float)(-(logZ2[z] + (double)kap * (Oa + U[z])));
@@ -500,13 +498,33 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
                 for (int jj = 0; jj < kJPT; ++jj) {
                     const int j = jg[jj];
+                    const int jl = tid + kNT * jj;
+                    // my butterfly's inputs (minus the global minimum) and history values
+                    float bin[4] = {0.f, 0.f, 0.f, 0.f}, bbin[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (in) {
+                        const float4 v = *reinterpret_cast<const float4 *>(in + 4 * jl);
+                        bin[0] = v.x - sigma; bin[1] = v.y - sigma;
+                        bin[2] = v.z - sigma; bin[3] = v.w - sigma;
+                        if (GRAD) {
+                            const float4 u = *reinterpret_cast<const float4 *>(in + kIn + 4 * jl);
+                            bbin[0] = u.x; bbin[1] = u.y; bbin[2] = u.z; bbin[3] = u.w;
+                        }
+                    }
+                    float a4[4] = {a0, a0, a0, a0}, h4[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (hrow) {
+#pragma unroll
+                        for (int p = 0; p < 4; ++p) {
+                            a4[p] = sm.hst[z][0][p * kJPC + jl];
+                            if (GRAD) h4[p] = sm.hst[z][kPlanes - 1][p * kJPC + jl];
+                        }
+                    }
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {          // output groups p' = 2h, 2h+1
                         F2 xc[4];
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
                             const F2 d = sub2(cq[jj][c][h], W);
-                            xc[c] = fma2(d, d, bc(bin[jj][c]));
+                            xc[c] = fma2(d, d, bc(bin[c]));
                         }
                         const F2 M = mk(min4(xc[0].x, xc[1].x, xc[2].x, xc[3].x),
                                         min4(xc[0].y, xc[1].y, xc[2].y, xc[3].y));
@@ -515,7 +533,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
                         for (int c = 0; c < 4; ++c) e[c] = ex2p(fma2(xc[c], NK, KM));
                         const F2 S = add2(add2(e[0], e[1]), add2(e[2], e[3]));
-                        const F2 f = ex2p(fma2(add2(M, mk(a4[jj][2 * h], a4[jj][2 * h + 1])), NK, CB));
+                        const F2 f = ex2p(fma2(add2(M, mk(a4[2 * h], a4[2 * h + 1])), NK, CB));
                         F2 ob = bc(0.f), bbo = bc(0.f);
                         if (t >= 0) {
                             ob = fma2(mk(lg2(S.x), lg2(S.y)), MIK, M);
@@ -527,11 +545,11 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                             for (int c = 1; c < 4; ++c) ec = fma2(e[c], cq[jj][c][h], ec);
                             acc = fma2(f, ec, acc);
                         } else {
-                            const F2 Hh = mk(h4[jj][2 * h], h4[jj][2 * h + 1]);
+                            const F2 Hh = mk(h4[2 * h], h4[2 * h + 1]);
                             F2 ey = bc(0.f), dl = bc(0.f);
 #pragma unroll
                             for (int c = 0; c < 4; ++c) {
-                                const F2 y = fma2(cq[jj][c][h], Gq, bc(bbin[jj][c] - gs));
+                                const F2 y = fma2(cq[jj][c][h], Gq, bc(bbin[c] - gs));
                                 ey = fma2(e[c], y, ey);
                                 const F2 cm = sub2(cq[jj][c][h], ST);
                                 dl = fma2(mul2(e[c], add2(y, Hh)), cm, dl);
@@ -540,13 +558,18 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                             acc = fma2(f, dl, acc);
                         }
                         if (t >= 0 && !failed) {
+                            // output Bt(p' 4096 + j) is input (j & 3) of butterfly
+                            // p' 1024 + (j >> 2): CTA p' kCL / 4, offset (p' 4096 + j) mod kIn
+                            const int d0 = (2 * h) * kCL / 4, d1 = (2 * h + 1) * kCL / 4;
+                            const uint32_t s0 = 4u * ((2 * h) % (4 / kCL)) * 4096u;
+                            const uint32_t s1 = 4u * ((2 * h + 1) % (4 / kCL)) * 4096u;
                             const uint32_t ob0 = buf_off + 4u * (uint32_t)j;
-                            st_async1(cbase[2 * h] + ob0, ob.x, cbase[2 * h] + bar_off);
-                            st_async1(cbase[2 * h + 1] + ob0, ob.y, cbase[2 * h + 1] + bar_off);
+                            st_async1(cbase[d0] + ob0 + s0, ob.x, cbase[d0] + bar_off);
+                            st_async1(cbase[d1] + ob0 + s1, ob.y, cbase[d1] + bar_off);
                             if (GRAD) {
-                                const uint32_t ob1 = ob0 + kNJ * 4;
-                                st_async1(cbase[2 * h] + ob1, bbo.x, cbase[2 * h] + bar_off);
-                                st_async1(cbase[2 * h + 1] + ob1, bbo.y, cbase[2 * h + 1] + bar_off);
+                                const uint32_t ob1 = ob0 + kIn * 4;
+                                st_async1(cbase[d0] + ob1 + s0, bbo.x, cbase[d0] + bar_off);
+                                st_async1(cbase[d1] + ob1 + s1, bbo.y, cbase[d1] + bar_off);
                             }
                         }
                     }
@@ -638,9 +661,16 @@ bool l16_applicable(int B, int N, int L, int BB, int V) {
     return L == l16::kL && BB == l16::kB && V == 1 && N >= 2 && N <= l16::kNMax;
 }
 
+namespace {
+int l16_slots(int mode) {
+    return mode == kModeBackward ? l16::SlotsOf<true>::value : l16::SlotsOf<false>::value;
+}
+}  // namespace
+
 int l16_clusters(int B, int mode) {
     const int maxc = (mode == kModeBackward) ? l16_max_clusters<true>() : l16_max_clusters<false>();
-    const long pairs = ((long)B + l16::kSlots - 1) / l16::kSlots;
+    const int slots = l16_slots(mode);
+    const long pairs = ((long)B + slots - 1) / slots;
     long n = maxc;
     if (n > pairs) n = pairs;
     return (int)n;
@@ -650,7 +680,7 @@ size_t l16_workspace_bytes(int B, int N, int mode) {
     const int ncl = l16_clusters(B, mode);
     if (ncl <= 0) return 0;
     const long slot = l16::slot_layout(N, mode == kModeBackward).total;
-    return (size_t)ncl * l16::kSlots * slot * 4;
+    return (size_t)ncl * l16_slots(mode) * slot * 4;
 }
 
 cudaError_t launch_l16(const LaunchArgs &a) {
@@ -658,7 +688,7 @@ cudaError_t launch_l16(const LaunchArgs &a) {
     const int ncl = l16_clusters(a.B, a.mode);
     if (ncl <= 0) return cudaErrorInvalidConfiguration;
     const long slot = l16::slot_layout(a.N, grad).total;
-    if ((size_t)ncl * l16::kSlots * slot * 4 > a.ws_data_bytes) return cudaErrorInvalidValue;
+    if ((size_t)ncl * l16_slots(a.mode) * slot * 4 > a.ws_data_bytes) return cudaErrorInvalidValue;
     const dim3 grid((unsigned)(ncl * l16::kCL)), block(l16::kNT);
     float *ws = reinterpret_cast<float *>(a.ws_data);
     if (grad) {
