@@ -96,16 +96,22 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // try_wait compiles to) takes issue slots from the warps that have work,
 // and measured on B200 a fixed ~400 ns sleep ran both cluster kernels
 // ~15 % faster than a suspending try_wait (shorter sleeps poll too often,
-// 800 ns and more oversleep).
-constexpr unsigned kWaitSleepNs = 400;
+// 800 ns and more oversleep).  A kernel with a single sequence in flight has
+// nothing else to run while it waits, and prefers a shorter sleep (template
+// argument).
+#ifndef BCJR_WAIT_SLEEP_NS
+#define BCJR_WAIT_SLEEP_NS 400
+#endif
+constexpr unsigned kWaitSleepNs = BCJR_WAIT_SLEEP_NS;
 
+template <unsigned kSleepNs = kWaitSleepNs>
 __device__ __forceinline__ void wait_bar(uint32_t bar, uint32_t parity, int *status,
                                          bool &failed) {
     if (failed) return;
     if (mbar_test(bar, parity)) return;
     const unsigned long long t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
-        __nanosleep(kWaitSleepNs);
+        if (kSleepNs) __nanosleep(kSleepNs);
         if (mbar_test(bar, parity)) return;
         if ((i & 7) == 0) {
             if (*reinterpret_cast<volatile int *>(status) != 0) {

@@ -84,6 +84,16 @@ struct SlotsOf {
     static constexpr int value = (kCL == 2 && GRAD) ? 1 : 2;
 };
 constexpr int kNMax = 512;            // longest sequence staged in shared memory
+// Sleep between tests of a bounded wait: a kernel with one slot in flight
+// has no other work while it waits: it polls without sleeping (measured on
+// B200: backward 117 ms with no sleep, 119 ms at 100 ns, 125 ms at 400 ns).
+#ifndef BCJR_L16_SLEEP1_NS
+#define BCJR_L16_SLEEP1_NS 0
+#endif
+template <bool GRAD>
+struct SleepOf {
+    static constexpr unsigned value = SlotsOf<GRAD>::value == 1 ? BCJR_L16_SLEEP1_NS : kWaitSleepNs;
+};
 constexpr int kWarps = kNT / 32;
 
 template <bool GRAD>
@@ -326,7 +336,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     const int x = use[z] & 1;
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
-                    wait_bar(bar, (use[z] >> 1) & 1, status, failed);
+                    wait_bar<SleepOf<GRAD>::value>(bar, (use[z] >> 1) & 1, status, failed);
                     shift = cluster_min(sm.maxslot[z][x]);
                     in = &sm.buf[z][x][0][0];
                     ++use[z];
@@ -468,7 +478,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     const int x = use[z] & 1;
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
-                    wait_bar(bar, (use[z] >> 1) & 1, status, failed);
+                    wait_bar<SleepOf<GRAD>::value>(bar, (use[z] >> 1) & 1, status, failed);
                     sigma = cluster_min(sm.maxslot[z][x]);
                     in = &sm.buf[z][x][0][0];
                     ++use[z];
@@ -476,7 +486,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 U[z] += (double)sigma;
                 const bool hrow = tn > 0;    // this step's alpha / H rows are staged
                 if (hrow) {
-                    wait_bar(sbase + soff(&sm.hbar[z]), hcnt[z] & 1, status, failed);
+                    wait_bar<SleepOf<GRAD>::value>(sbase + soff(&sm.hbar[z]), hcnt[z] & 1, status, failed);
                     ++hcnt[z];
                 }
                 const double Oa = tn > 0 ? sm.offs[z][tn - 1] : 0.0;
@@ -609,7 +619,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
         for (int z = 0; z < kSlots; ++z)
             for (uint32_t k = hcnt[z]; k < (uint32_t)sm.hiss[z]; ++k)
-                wait_bar(sbase + soff(&sm.hbar[z]), k & 1, status, f2);
+                wait_bar<SleepOf<GRAD>::value>(sbase + soff(&sm.hbar[z]), k & 1, status, f2);
     }
     cluster_sync();
 }
