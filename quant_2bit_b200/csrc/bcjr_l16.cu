@@ -103,7 +103,7 @@ struct alignas(128) Smem {
     float buf[kSlots][2][kPlanes][kIn];   // input ring (kIn floats per plane)
     float hst[kSlots][kPlanes][kIn];      // history rows staged by TMA: [p * kJPC + jl]
     double offs[kSlots][kNMax];           // alpha shifts O_t
-    float maxslot[kSlots][2][kCL];        // per-CTA minimum cost riding with the data
+    float maxslot[kSlots][2][kCL * kWarps];   // per-warp minimum cost riding with the data
     float w[kSlots][kNMax];
     float g[kSlots][GRAD ? kNMax : 4];
     float sf[kSlots][GRAD ? kNMax : 4];
@@ -112,19 +112,17 @@ struct alignas(128) Smem {
     float lz[kSlots][kCL][2];
     unsigned long long full[kSlots][2];
     unsigned long long hbar[kSlots];
-    int mn[kSlots][2];                    // per-step CTA minimum (order-preserving int key)
-    int cnt[kSlots][2];                   // warps finished with the step
+    int cnt[kSlots][2];                   // warps finished with the step (backward sweep)
     int hiss[kSlots];                     // TMA row loads issued per slot
 };
 
-// Minimum of the kCL per-CTA minima riding with a consumption.
-__device__ __forceinline__ float cluster_min(const float *m) {
-    if (kCL == 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(m);
-        return min4(v.x, v.y, v.z, v.w);
-    }
-    const float2 v = *reinterpret_cast<const float2 *>(m);
-    return fminf(v.x, v.y);
+// Minimum of the kCL * kWarps per-warp minima riding with a consumption
+// (called by whole warps).
+__device__ __forceinline__ float cluster_min(const float *m, int lane) {
+    float v = m[lane];
+#pragma unroll
+    for (int i = 32; i < kCL * kWarps; i += 32) v = fminf(v, m[lane + i]);
+    return redux_min(v);
 }
 
 // Workspace of one (cluster, slot): float offsets.
@@ -157,7 +155,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     SM &sm = *reinterpret_cast<SM *>(smem_raw);
     constexpr int kPlanes = SM::kPlanes;
     constexpr int kSlots = SM::kSlots;
-    constexpr uint32_t kBytes = kPlanes * kIn * 4 + kCL * 4;   // per consumption
+    constexpr uint32_t kBytes = kPlanes * kIn * 4 + kCL * kWarps * 4;   // per consumption
     constexpr uint32_t kRowBytes = kJPC * 4;                    // one TMA chunk
 
     const int tid = threadIdx.x;
@@ -218,7 +216,6 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         for (int z = 0; z < kSlots; ++z) {
             sm.hiss[z] = 0;
             for (int x = 0; x < 2; ++x) {
-                sm.mn[z][x] = order_key(kPosInf);
                 sm.cnt[z][x] = 0;
             }
         }
@@ -264,31 +261,33 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 
     auto finish_step = [&](int z, int nb, bool send, float lmin, float *part_row, float acc,
                            int rows_tn, float *const *slot_ws) {
-        // warp minimum with one redux.sync on the order-preserving integer key
-        // warp minimum with one float redux.sync (sm_100a); integer key for the smem atomic
+        // The warp's minimum output cost goes to every consumer CTA with the
+        // data (part of the consumption's byte count).  Sent after the warp
+        // has read this step's inputs, it also tells every producer that the
+        // warp is done with the ring buffer the producer writes next.
         const float wmin = send ? redux_min(lmin) : 0.f;
+        if (send && lane < kCL && !failed) {
+            const uint32_t peer = mapa(sbase, (uint32_t)lane);
+            st_async1(peer + soff(&sm.maxslot[z][nb][rank * kWarps + warp]), wmin,
+                      peer + soff(&sm.full[z][nb]));
+        }
         if (part_row) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0) part_row[warp] = acc;
         }
-        int last = 0;
-        if (lane == 0) {
-            if (part_row) part_row[warp] = acc;
-            if (send) atomicMin(&sm.mn[z][nb], order_key(wmin));
-            __threadfence_block();
-            last = atomicAdd(&sm.cnt[z][nb], 1) == kWarps - 1;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-            __threadfence_block();
-            const int k = atomicOr(&sm.mn[z][nb], 0);
-            if (send && lane < kCL && !failed)
-                st_async1(cbase[lane] + soff(&sm.maxslot[z][nb][rank]), order_key_inv(k),
-                          cbase[lane] + soff(&sm.full[z][nb]));
-            if (rows_tn >= 1 && lane == 0) issue_rows(z, rows_tn, slot_ws);
-            __syncwarp();
+        if (rows_tn >= 1) {
+            // the last warp to finish the step has the staged history row to
+            // itself: it loads the next one
+            int last = 0;
             if (lane == 0) {
-                sm.mn[z][nb] = order_key(kPosInf);
+                __threadfence_block();
+                last = atomicAdd(&sm.cnt[z][nb], 1) == kWarps - 1;
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last && lane == 0) {
+                __threadfence_block();
+                issue_rows(z, rows_tn, slot_ws);
                 sm.cnt[z][nb] = 0;
             }
         }
@@ -337,7 +336,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
                     wait_bar<SleepOf<GRAD>::value>(bar, (use[z] >> 1) & 1, status, failed);
-                    shift = cluster_min(sm.maxslot[z][x]);
+                    shift = cluster_min(sm.maxslot[z][x], lane);
                     in = &sm.buf[z][x][0][0];
                     ++use[z];
                 }
@@ -479,7 +478,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
                     wait_bar<SleepOf<GRAD>::value>(bar, (use[z] >> 1) & 1, status, failed);
-                    sigma = cluster_min(sm.maxslot[z][x]);
+                    sigma = cluster_min(sm.maxslot[z][x], lane);
                     in = &sm.buf[z][x][0][0];
                     ++use[z];
                 }
