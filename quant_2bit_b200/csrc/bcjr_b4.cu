@@ -32,7 +32,7 @@
 // --------------------
 // Producers push outputs into the consumer CTA's shared-memory ring with
 // st.async ... mbarrier::complete_tx (double-buffered, byte-counted, bounded
-// waits, free-running warps with a last-arriver that ships the CTA minimum;
+// waits, free-running warps that ship their minimum cost with their data;
 // see bcjr_l16.cu).  Each warp's outputs go to one consumer CTA as one
 // contiguous 256-byte block:
 //   alpha ring [p/2][64 butterflies][p%2]: a thread's two outputs are the
@@ -90,7 +90,7 @@ struct alignas(128) Smem {
     float hst[kSlots][kPlanes][kIn];      // history chunk staged by TMA (alpha layout)
     float zero[kPlanes][kIn];             // all-zero inputs of the first step of each sweep
     double offs[kSlots][kNMax];           // alpha shifts O_t
-    float maxslot[kSlots][2][kCL];        // per-CTA minimum cost riding with the data
+    float maxslot[kSlots][2][kCL * kWarps];   // per-warp minimum cost riding with the data
     float2 w[kSlots][kNMax];
     float2 g[kSlots][GRAD ? kNMax : 1];
     float2 sf[kSlots][GRAD ? kNMax : 1];
@@ -99,8 +99,7 @@ struct alignas(128) Smem {
     float lz[kSlots][kCL][2];
     unsigned long long full[kSlots][2];
     unsigned long long hbar[kSlots];
-    int mn[kSlots][2];                    // per-step CTA minimum (order-preserving int key)
-    int cnt[kSlots][2];                   // warps finished with the step
+    int cnt[kSlots][2];                   // warps finished with the step (backward sweep)
     int hiss[kSlots];                     // TMA row loads issued per slot
 };
 
@@ -108,6 +107,15 @@ struct alignas(128) Smem {
 __device__ __forceinline__ uint32_t beta_off(uint32_t rl, uint32_t c) {
     const uint32_t chunk = (((rl & 1u) << 2) | (c >> 2)) ^ ((rl >> 1) & 7u);
     return (rl >> 1) * 32u + chunk * 4u + (c & 3u);
+}
+
+// Minimum of the kCL * kWarps per-warp minima riding with a consumption
+// (called by whole warps).
+__device__ __forceinline__ float cluster_min(const float *m, int lane) {
+    float v = m[lane];
+#pragma unroll
+    for (int i = 32; i < kCL * kWarps; i += 32) v = fminf(v, m[lane + i]);
+    return redux_min(v);
 }
 
 __device__ __forceinline__ float min16(const F2 (&x)[8]) {
@@ -151,7 +159,7 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     using SM = Smem<GRAD>;
     SM &sm = *reinterpret_cast<SM *>(smem_raw);
     constexpr int kPlanes = SM::kPlanes;
-    constexpr uint32_t kBytes = kPlanes * kIn * 4 + kCL * 4;   // per consumption
+    constexpr uint32_t kBytes = kPlanes * kIn * 4 + kCL * kWarps * 4;   // per consumption
     constexpr uint32_t kChunkBytes = kPlanes * kIn * 4;          // history chunk per CTA
     constexpr long kRowFloats = (long)kCL * kPlanes * kIn;
 
@@ -243,7 +251,6 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         for (int z = 0; z < kSlots; ++z) {
             sm.hiss[z] = 0;
             for (int x = 0; x < 2; ++x) {
-                sm.mn[z][x] = order_key(kPosInf);
                 sm.cnt[z][x] = 0;
             }
         }
@@ -281,7 +288,16 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     // to the four consumers and, in the beta sweep, issues the next TMA row.
     auto finish_step = [&](int z, int nb, bool send, float lmin, float *part_row, F2 acc,
                            int rows_tn, float *const *slot_ws) {
+        // The warp's minimum output cost goes to every consumer CTA with the
+        // data (part of the consumption's byte count).  Sent after the warp
+        // has read this step's inputs, it also tells every producer that the
+        // warp is done with the ring buffer the producer writes next.
         const float wmin = send ? redux_min(lmin) : 0.f;
+        if (send && lane < kCL && !failed) {
+            const uint32_t peer = mapa(sbase, (uint32_t)lane);
+            st_async1(peer + soff(&sm.maxslot[z][nb][rank * kWarps + warp]), wmin,
+                      peer + soff(&sm.full[z][nb]));
+        }
         if (part_row) {
             // lanes 0-15 reduce component 0, lanes 16-31 component 1
             const bool hi = lane >= 16;
@@ -291,25 +307,18 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
             if ((lane & 15) == 0) part_row[2 * warp + (lane >> 4)] = keep;
         }
-        int last = 0;
-        if (lane == 0) {
-            if (send) atomicMin(&sm.mn[z][nb], order_key(wmin));
-            __threadfence_block();
-            last = atomicAdd(&sm.cnt[z][nb], 1) == kWarps - 1;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-            __threadfence_block();
-            const int k = atomicOr(&sm.mn[z][nb], 0);
-            if (send && lane < kCL && !failed) {
-                const uint32_t peer = mapa(sbase, (uint32_t)lane);
-                st_async1(peer + soff(&sm.maxslot[z][nb][rank]), order_key_inv(k),
-                          peer + soff(&sm.full[z][nb]));
-            }
-            if (rows_tn >= 1 && lane == 0) issue_rows(z, rows_tn, slot_ws);
-            __syncwarp();
+        if (rows_tn >= 1) {
+            // the last warp to finish the step has the staged history row to
+            // itself: it loads the next one
+            int last = 0;
             if (lane == 0) {
-                sm.mn[z][nb] = order_key(kPosInf);
+                __threadfence_block();
+                last = atomicAdd(&sm.cnt[z][nb], 1) == kWarps - 1;
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last && lane == 0) {
+                __threadfence_block();
+                issue_rows(z, rows_tn, slot_ws);
                 sm.cnt[z][nb] = 0;
             }
         }
@@ -362,8 +371,7 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
                     wait_bar(bar, (use[z] >> 1) & 1, status, failed);
-                    const float4 mx = *reinterpret_cast<const float4 *>(sm.maxslot[z][x]);
-                    shift = sub = min4(mx.x, mx.y, mx.z, mx.w);
+                    shift = sub = cluster_min(sm.maxslot[z][x], lane);
                     in = &sm.buf[z][x][0][0];
                     ++use[z];
                 }
@@ -504,8 +512,7 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
                     wait_bar(bar, (use[z] >> 1) & 1, status, failed);
-                    const float4 mx = *reinterpret_cast<const float4 *>(sm.maxslot[z][x]);
-                    sigma = min4(mx.x, mx.y, mx.z, mx.w);
+                    sigma = cluster_min(sm.maxslot[z][x], lane);
                     in = &sm.buf[z][x][0][0];
                     ++use[z];
                 }

@@ -34,18 +34,19 @@
 // consumer CTA's shared memory with st.async ... mbarrier::complete_tx, into
 // a double-buffered ring; the consumer arms each buffer's mbarrier with the
 // expected byte count.  There is no block barrier per step: each warp that
-// finishes a step folds its minimum output cost into a shared-memory minimum
-// and counts itself in; the last warp of the CTA sends the CTA minimum to
-// every consumer, as part of the same consumption's byte count.  A producer
-// that has received the complete input of consumption u therefore knows
-// that every warp of every CTA has finished reading consumption u-1, whose
-// buffer it is about to overwrite.  Every consumer renormalises by the exact
-// global minimum of the previous step; shifts accumulate in double.
+// finishes a step sends its minimum output cost to every consumer CTA along
+// with its data, as part of the same consumption's byte count, and every
+// consumer warp takes the minimum over all of them with one redux.  A
+// producer that has received the complete input of consumption u therefore
+// knows that every warp of every CTA has finished reading consumption u-1,
+// whose buffer it is about to overwrite.  Every consumer renormalises by the
+// exact global minimum of the previous step; shifts accumulate in double.
 //
 // Two sequences ("slots") are interleaved step by step so that one slot's
 // exchange latency hides behind the other's arithmetic (one in the 2-CTA
-// backward: its two 32 KB planes per ring buffer fill shared memory).  Alpha / H rows go
-// to a global history with float4 stores; the backward-time sweep fetches
+// backward: its two 32 KB planes per ring buffer fill shared memory).
+// Alpha / H rows go to a global history with float4 stores; the
+// backward-time sweep fetches
 // the rows it needs one step ahead with TMA bulk copies (cp.async.bulk) into
 // shared memory.  Per-step partial sums of soft / d_seq are written per CTA
 // and added in a fixed order by CTA 0: results are deterministic.
