@@ -528,13 +528,20 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                             if (GRAD) h4[p] = sm.hst[z][kPlanes - 1][p * kJPC + jl];
                         }
                     }
+                    // inputs shared by both output-group pairs, as f32x2 broadcasts
+                    F2 Bb[4], Yb[4];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        Bb[c] = bc(bin[c]);
+                        Yb[c] = bc(bbin[c] - gs);
+                    }
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {          // output groups p' = 2h, 2h+1
                         F2 xc[4];
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
                             const F2 d = sub2(cq[jj][c][h], W);
-                            xc[c] = fma2(d, d, bc(bin[c]));
+                            xc[c] = fma2(d, d, Bb[c]);
                         }
                         const F2 M = mk(min4(xc[0].x, xc[1].x, xc[2].x, xc[3].x),
                                         min4(xc[0].y, xc[1].y, xc[2].y, xc[3].y));
@@ -559,7 +566,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                             F2 ey = bc(0.f), dl = bc(0.f);
 #pragma unroll
                             for (int c = 0; c < 4; ++c) {
-                                const F2 y = fma2(cq[jj][c][h], Gq, bc(bbin[c] - gs));
+                                const F2 y = fma2(cq[jj][c][h], Gq, Yb[c]);
                                 ey = fma2(e[c], y, ey);
                                 const F2 cm = sub2(cq[jj][c][h], ST);
                                 dl = fma2(mul2(e[c], add2(y, Hh)), cm, dl);
