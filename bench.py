@@ -51,11 +51,13 @@ SHAPES = {"c2": (1, 256), "c3": (1, 256), "c5": (1, 256), "v2": (2, 128)}
 MUFU = {1: (3.5, 4.0), 2: (3.125, 3.25)}
 MUFU_PER_SM_CLK = 16
 # dram__bytes_read.sum + dram__bytes_write.sum per sequence of the cluster
-# kernels from one ncu capture of a 148-sequence launch (profiles/); traffic
-# grows in proportion to sequences.  V=1: L=16, N=256.
-DRAM_BYTES_PER_SEQ = {1: {"forward": (2.222191e9 + 2.488541e9) / 148,
-                          "backward": (4.726516e9 + 4.964882e9) / 148},
-                      2: None}
+# kernels, from one ncu capture of a 296-sequence launch of each
+# (profiles/); traffic grows in proportion to sequences.  V=1: L=16, N=256
+# (2-CTA clusters); V=2: L=16, N=128 (the history rows mostly stay in L2).
+DRAM_BYTES_PER_SEQ = {1: {"forward": (4.822843e9 + 4.961722e9) / 296,
+                          "backward": (9.663011e9 + 9.910032e9) / 296},
+                      2: {"forward": (0.219314e9 + 0.564500e9) / 296,
+                          "backward": (0.830065e9 + 1.220563e9) / 296}}
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -391,7 +393,7 @@ def main():
             "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "Gop/s", "frac": achieved / peak,
                          "traffic": DRAM_BYTES_PER_SEQ[V][dom] * Bl if DRAM_BYTES_PER_SEQ[V] else None,
-                         "traffic_unit": "bytes per launch (ncu, 148-sequence capture scaled by "
+                         "traffic_unit": "bytes per launch (ncu, 296-sequence capture scaled by "
                                          "sequences; see profiles/)",
                          "note": f"algorithmic MUFU ops: {MUFU_FWD}/{MUFU_BWD} per state-step "
                                  f"(fwd/bwd call), peak = {sms} SMs x 16/clk x {clk_mhz:.0f} MHz"},
