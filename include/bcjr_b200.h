@@ -145,6 +145,49 @@ BCJR_API int bcjr_fb_forward_noalloc(const float *seq, const float *cb, const fl
                                      int B, int N, int L, int k, int V,
                                      float *soft, float *logZ, bcjr_stream_t stream);
 
+/*
+ * Randomized Hadamard transform and tiling around the op: the caller side
+ * of the reference's quantizer wrapper.  m, n are powers of two in
+ * [16, 32768]; fp32 matrices row-major; sign vectors of +-1 (length m for
+ * sign_l, n for sign_r); workspace of bcjr_rht_workspace_bytes(m, n) bytes,
+ * 256-byte aligned.  Stream-ordered, no host synchronisation.
+ *
+ * bcjr_rht: out = H_m diag(sign_l) W diag(sign_r) H_n / sqrt(m n) (inverse
+ * = 0), or its inverse diag(sign_l) H_m W H_n diag(sign_r) / sqrt(m n)
+ * (inverse = 1), H the unnormalised Walsh-Hadamard matrix.  Replaces
+ * apply_rht_gpu / apply_inverse_rht_gpu (src/qat/ste.py:113-135, which need
+ * the fast_hadamard_transform extension) and apply_rht / apply_inverse_rht
+ * (src/rht/transform.py:65-126).
+ */
+BCJR_API size_t bcjr_rht_workspace_bytes(int m, int n);
+BCJR_API int bcjr_rht(const float *W, const float *sign_l, const float *sign_r, int m, int n,
+                      int inverse, float *out, void *ws, size_t ws_bytes, bcjr_stream_t stream);
+
+/*
+ * seqs (m n / 256 sequences of 256) = tile(RHT(W)) * mu, in the 16 x 16 tile
+ * order of _tile_for_viterbi_gpu (src/qat/ste.py:138-149): sequence
+ * j (m/16) + i holds rows 16i.., cols 16j.., row-major.  mu_dev NULL: mu =
+ * 1 / max(RMS(RHT(W)), 1e-30), the detached RMS scale of
+ * bcjr_quantize_weight_rotated (src/bcjr/bcjr_quant.py:125-141); the RMS is
+ * written to rms_out when it is not NULL (device float).  Otherwise mu is
+ * read from mu_dev (device float) and rms_out is ignored.
+ */
+BCJR_API int bcjr_rht_tile(const float *W, const float *sign_l, const float *sign_r, int m, int n,
+                           const float *mu_dev, float *seqs, float *rms_out, void *ws,
+                           size_t ws_bytes, bcjr_stream_t stream);
+
+/*
+ * out (m x n) = RHT^-1(untile(seqs) * s), s read from s_dev (device float):
+ * the untile, rescale and inverse RHT that follow the op in
+ * bcjr_quantize_weight_rotated / bcjr_quantize_weight
+ * (src/bcjr/bcjr_quant.py:149-178, src/qat/ste.py:152-159).  It is also the
+ * adjoint of bcjr_rht_tile with mu = s, and bcjr_rht_tile with mu = s is its
+ * adjoint (gradients of the pair).
+ */
+BCJR_API int bcjr_untile_irht(const float *seqs, const float *sign_l, const float *sign_r, int m,
+                              int n, const float *s_dev, float *out, void *ws, size_t ws_bytes,
+                              bcjr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

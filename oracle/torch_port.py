@@ -116,3 +116,36 @@ def internals(seq, cb, T, L, k, V):
     logZ = torch.logsumexp(la[:, -1], dim=-1)
     P = (la + lb - logZ.view(-1, 1, 1)).exp()
     return P, la, lb
+
+
+# ---------------------------------------------------------------------------
+# Caller side (differentiable torch restatement, for the wrapper's gradient
+# checks): randomized Hadamard transform of src/rht/transform.py:24-126 and
+# the rotated pipeline of src/bcjr/bcjr_quant.py:125-178.
+
+def fwht(x):
+    """Unscaled Walsh-Hadamard transform along the last axis (power of two)."""
+    n = x.shape[-1]
+    shape = x.shape
+    y = x.reshape(-1, n)
+    h = 1
+    while h < n:
+        y = y.reshape(-1, n // (2 * h), 2, h)
+        a, b = y[:, :, 0, :], y[:, :, 1, :]
+        y = torch.stack((a + b, a - b), dim=2)
+        h *= 2
+    return y.reshape(shape)
+
+
+def apply_rht(W, sign_l, sign_r):
+    m, n = W.shape
+    Wr = fwht(W * sign_r.unsqueeze(0))
+    Wl = fwht((Wr * sign_l.unsqueeze(1)).transpose(0, 1)).transpose(0, 1)
+    return Wl / (m * n) ** 0.5
+
+
+def apply_inverse_rht(Wt, sign_l, sign_r):
+    m, n = Wt.shape
+    Wr = fwht(Wt) * sign_r.unsqueeze(0)
+    Wl = fwht(Wr.transpose(0, 1)).transpose(0, 1) * sign_l.unsqueeze(1)
+    return Wl / (m * n) ** 0.5

@@ -15,6 +15,11 @@ LIB_PATH = os.path.join(HERE, "libbcjr_b200.so")
 BCJR_OK = 0
 BCJR_ERR_BAD_SHAPE = 1
 BCJR_ERR_UNSUPPORTED = 2
+BCJR_ERR_NULL_POINTER = 3
+BCJR_ERR_ALIGNMENT = 4
+BCJR_ERR_WORKSPACE = 5
+BCJR_ERR_LAUNCH = 6
+BCJR_ERR_DEVICE = 7
 BCJR_ERR_TIMEOUT = 8
 WS_FORWARD, WS_BACKWARD, WS_INTERNALS = 1, 2, 4
 
@@ -32,6 +37,10 @@ SIGNATURES = {
     "bcjr_fb_internals": ([_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P], _I),
     "bcjr_ws_status": ([_P, _P], _I),
     "bcjr_fb_forward_noalloc": ([_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P], _I),
+    "bcjr_rht_workspace_bytes": ([_I, _I], _SZ),
+    "bcjr_rht": ([_P, _P, _P, _I, _I, _I, _P, _P, _SZ, _P], _I),
+    "bcjr_rht_tile": ([_P, _P, _P, _I, _I, _P, _P, _P, _P, _SZ, _P], _I),
+    "bcjr_untile_irht": ([_P, _P, _P, _I, _I, _P, _P, _P, _SZ, _P], _I),
 }
 
 _lib = None

@@ -11,16 +11,21 @@ Differences that do not change results:
 * ``chunk_size`` / ``use_checkpoint`` are accepted and ignored: the op keeps
   no per-tile (N, 2^L) buffers (the reference chunks to bound those, and
   checkpoints to drop them), so every tile goes through one launch.
-* The randomized Hadamard transform uses a torch fast Walsh-Hadamard
-  transform (``fwht``) instead of the un-vendored fast_hadamard_transform
-  extension the reference requires (src/qat/ste.py:34-38, :118); same
-  unnormalised transform, same 1/sqrt(mn) scaling (src/rht/transform.py:65-126).
+* The randomized Hadamard transform, RMS scale and tiling run as native
+  kernels (csrc/bcjr_rht.cu) instead of the un-vendored
+  fast_hadamard_transform extension the reference requires
+  (src/qat/ste.py:34-38, :118): same unnormalised transform, same 1/sqrt(mn)
+  scaling (src/rht/transform.py:65-126), same detached RMS scale and tile
+  order.  ``bcjr_quantize_weight`` runs RHT + scale + tile as one call and
+  untile + rescale + inverse RHT as another; each is the other's adjoint, so
+  their backward passes are the same two calls.
 """
 import math
 
 import numpy as np
 import torch
 
+from . import _lib
 from .bcjr import (K_BITS, L_BITS, V_DIM, BcjrForwardBackwardMonolithic,
                    build_pred_succ_tables)
 
@@ -35,36 +40,128 @@ def make_sign_vector(n, seed):
     return rng.choice([-1.0, 1.0], size=n).astype(np.float32)
 
 
-def fwht(x):
-    """Unscaled fast Walsh-Hadamard transform along the last axis (length a
-    power of two), in the butterfly order of src/rht/transform.py:26-40."""
-    n = x.shape[-1]
-    assert n > 0 and (n & (n - 1)) == 0, f"FWHT length must be a power of 2, got {n}"
-    shape = x.shape
-    y = x.reshape(-1, n)
-    h = 1
-    while h < n:
-        y = y.view(-1, n // (2 * h), 2, h)
-        a, b = y[:, :, 0, :], y[:, :, 1, :]
-        y = torch.stack((a + b, a - b), dim=2)
-        h *= 2
-    return y.reshape(shape)
+def _rht_args(W, sign_l, sign_r):
+    if not (W.is_cuda and sign_l.is_cuda and sign_r.is_cuda):
+        raise RuntimeError("the RHT kernels need CUDA tensors (there is no CPU path)")
+    assert W.dim() == 2, "W must be (m, n)"
+    m, n = W.shape
+    for v, name in ((m, "m"), (n, "n")):
+        assert v >= 16 and v <= 32768 and v & (v - 1) == 0, \
+            f"FWHT length must be a power of 2 in [16, 32768], got {name}={v}"
+    assert sign_l.numel() == m and sign_r.numel() == n, "sign vectors must have lengths m and n"
+    return (W.detach().float().contiguous(), sign_l.detach().float().contiguous().view(-1),
+            sign_r.detach().float().contiguous().view(-1), m, n)
+
+
+def _rht_ws(m, n, device):
+    lib = _lib.load()
+    nbytes = lib.bcjr_rht_workspace_bytes(m, n)
+    if nbytes == 0:
+        raise ValueError(f"unsupported RHT shape ({m}, {n})")
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def _rht_call(W, sl, sr, m, n, inverse):
+    lib = _lib.load()
+    out = torch.empty((m, n), dtype=torch.float32, device=W.device)
+    ws = _rht_ws(m, n, W.device)
+    P = _lib.ptr
+    _lib.check(lib.bcjr_rht(P(W), P(sl), P(sr), m, n, int(inverse), P(out), P(ws), ws.numel(),
+                            _lib.stream_ptr(W.device)), "bcjr_rht")
+    return out
+
+
+def _tile_call(W, sl, sr, m, n, mu=None):
+    """(seqs (m n / 256, 256), rms) = tile(RHT(W)) * mu; mu = 1 / rms if None."""
+    lib = _lib.load()
+    seqs = torch.empty((m * n // 256, 256), dtype=torch.float32, device=W.device)
+    rms = torch.empty((), dtype=torch.float32, device=W.device)
+    ws = _rht_ws(m, n, W.device)
+    P = _lib.ptr
+    _lib.check(lib.bcjr_rht_tile(P(W), P(sl), P(sr), m, n, P(mu) if mu is not None else None,
+                                 P(seqs), P(rms), P(ws), ws.numel(), _lib.stream_ptr(W.device)),
+               "bcjr_rht_tile")
+    return seqs, rms
+
+
+def _untile_call(S, sl, sr, m, n, s):
+    """RHT^-1(untile(S) * s)."""
+    lib = _lib.load()
+    out = torch.empty((m, n), dtype=torch.float32, device=S.device)
+    ws = _rht_ws(m, n, S.device)
+    P = _lib.ptr
+    _lib.check(lib.bcjr_untile_irht(P(S), P(sl), P(sr), m, n, P(s), P(out), P(ws), ws.numel(),
+                                    _lib.stream_ptr(S.device)), "bcjr_untile_irht")
+    return out
+
+
+class _Rht(torch.autograd.Function):
+    """RHT (inverse=False) or its inverse; orthogonal, so each one's backward
+    is the other."""
+
+    @staticmethod
+    def forward(ctx, W, sign_l, sign_r, inverse):
+        Wc, sl, sr, m, n = _rht_args(W, sign_l, sign_r)
+        ctx.save_for_backward(sl, sr)
+        ctx.inverse = inverse
+        return _rht_call(Wc, sl, sr, m, n, inverse)
+
+    @staticmethod
+    def backward(ctx, g):
+        sl, sr = ctx.saved_tensors
+        m, n = g.shape
+        return _rht_call(g.float().contiguous(), sl, sr, m, n, not ctx.inverse), None, None, None
+
+
+class _RhtTile(torch.autograd.Function):
+    """(seqs, rms) = (tile(RHT(W)) / rms, rms), rms = RMS(RHT(W)) detached."""
+
+    @staticmethod
+    def forward(ctx, W, sign_l, sign_r):
+        Wc, sl, sr, m, n = _rht_args(W, sign_l, sign_r)
+        seqs, rms = _tile_call(Wc, sl, sr, m, n)
+        mu = 1.0 / rms
+        ctx.save_for_backward(sl, sr, mu)
+        ctx.mn = (m, n)
+        ctx.mark_non_differentiable(rms)
+        return seqs, rms
+
+    @staticmethod
+    def backward(ctx, g_seqs, g_rms):
+        sl, sr, mu = ctx.saved_tensors
+        m, n = ctx.mn
+        return _untile_call(g_seqs.float().contiguous(), sl, sr, m, n, mu), None, None
+
+
+class _UntileIrht(torch.autograd.Function):
+    """W = RHT^-1(untile(S) * s), s a detached device scalar."""
+
+    @staticmethod
+    def forward(ctx, S, sign_l, sign_r, s, m, n):
+        sl = sign_l.detach().float().contiguous().view(-1)
+        sr = sign_r.detach().float().contiguous().view(-1)
+        s = s.detach().float().contiguous()
+        ctx.save_for_backward(sl, sr, s)
+        ctx.mn = (m, n)
+        return _untile_call(S.float().contiguous(), sl, sr, m, n, s)
+
+    @staticmethod
+    def backward(ctx, g):
+        sl, sr, s = ctx.saved_tensors
+        m, n = ctx.mn
+        seqs, _ = _tile_call(g.float().contiguous(), sl, sr, m, n, mu=s)
+        return seqs, None, None, None, None, None
 
 
 def apply_rht_gpu(W, sign_l, sign_r):
-    """W~ = H_m diag(sign_l) W diag(sign_r) H_n / sqrt(mn) (src/qat/ste.py:113-125)."""
-    m, n = W.shape
-    Wr = fwht(W * sign_r.unsqueeze(0))
-    Wl = fwht((Wr * sign_l.unsqueeze(1)).transpose(0, 1).contiguous()).transpose(0, 1)
-    return Wl / math.sqrt(m * n)
+    """W~ = H_m diag(sign_l) W diag(sign_r) H_n / sqrt(mn) (src/qat/ste.py:113-125),
+    differentiable."""
+    return _Rht.apply(W, sign_l, sign_r, False)
 
 
 def apply_inverse_rht_gpu(W_tilde, sign_l, sign_r):
-    """Inverse of apply_rht_gpu (src/qat/ste.py:128-135)."""
-    m, n = W_tilde.shape
-    Wr = fwht(W_tilde) * sign_r.unsqueeze(0)
-    Wl = fwht(Wr.transpose(0, 1).contiguous()).transpose(0, 1) * sign_l.unsqueeze(1)
-    return Wl / math.sqrt(m * n)
+    """Inverse of apply_rht_gpu (src/qat/ste.py:128-135), differentiable."""
+    return _Rht.apply(W_tilde, sign_l, sign_r, True)
 
 
 def _tile_for_viterbi_gpu(W, Tx=TX, Ty=TY):
@@ -118,19 +215,29 @@ def bcjr_quantize_weight(W_latent, sign_l, sign_r, codebook, T_temp, preds=None,
                          chunk_size=BCJR_CHUNK, Tx=TX, Ty=TY):
     """RHT, BCJR quantize, inverse RHT (src/bcjr/bcjr_quant.py:159-178).  The
     pred/succ tables default to the codebook's trellis (L from its rows, V
-    from its columns, k = 2)."""
+    from its columns, k = 2).  With the default 16x16 tiles the RHT, RMS scale
+    and tiling run as one native call and the untile, rescale and inverse RHT
+    as another."""
     if preds is None or succs is None:
         L = int(round(math.log2(codebook.shape[0])))
         preds, succs = build_pred_succ_tables(L=L, k=K_BITS, V=codebook.shape[1],
                                               device=W_latent.device)
-    W_tilde = apply_rht_gpu(W_latent, sign_l, sign_r)
-    W_tilde_q = bcjr_quantize_weight_rotated(W_tilde, codebook, T_temp, preds, succs,
-                                             chunk_size=chunk_size, Tx=Tx, Ty=Ty)
-    return apply_inverse_rht_gpu(W_tilde_q, sign_l, sign_r)
+    if Tx != TX or Ty != TY:
+        W_tilde = apply_rht_gpu(W_latent, sign_l, sign_r)
+        W_tilde_q = bcjr_quantize_weight_rotated(W_tilde, codebook, T_temp, preds, succs,
+                                                 chunk_size=chunk_size, Tx=Tx, Ty=Ty)
+        return apply_inverse_rht_gpu(W_tilde_q, sign_l, sign_r)
+    m, n = W_latent.shape
+    V = codebook.shape[1]
+    seqs, rms = _RhtTile.apply(W_latent, sign_l, sign_r)
+    B = seqs.shape[0]
+    soft = bcjr_quantize_tiles(seqs.view(B, (TX * TY) // V, V), codebook, T_temp, preds, succs,
+                               chunk_size=chunk_size)
+    return _UntileIrht.apply(soft.reshape(B, TX * TY), sign_l, sign_r, rms, m, n)
 
 
 __all__ = [
-    "TX", "TY", "BCJR_CHUNK", "L_BITS", "K_BITS", "V_DIM", "make_sign_vector", "fwht",
+    "TX", "TY", "BCJR_CHUNK", "L_BITS", "K_BITS", "V_DIM", "make_sign_vector",
     "apply_rht_gpu", "apply_inverse_rht_gpu", "_tile_for_viterbi_gpu",
     "_untile_from_viterbi_gpu", "_bcjr_chunk_forward", "bcjr_quantize_tiles",
     "bcjr_quantize_weight_rotated", "bcjr_quantize_weight",

@@ -1,7 +1,8 @@
-"""Caller-side layer (quant_2bit_b200.quant, .hook): RHT, sign vectors and
-tile order against the reference's outputs (tests/golden/rht.npz), the hook
+"""Caller-side layer (quant_2bit_b200.quant, .hook): sign vectors and tile
+order against the reference's outputs (tests/golden/rht.npz), the hook
 against an importable reference checkout, and (GPU) the whole quantizer
-wrapper against the reference's eager algorithm on CPU."""
+wrapper, forward and gradient, against the reference's algorithm restated in
+torch on CPU (the native RHT kernels themselves: tests/test_gpu_rht.py)."""
 import os
 import sys
 
@@ -22,17 +23,6 @@ def test_sign_vectors_match_reference():
     d = _rht()
     np.testing.assert_array_equal(make_sign_vector(32, 5), d["sign_l"])
     np.testing.assert_array_equal(make_sign_vector(64, 6), d["sign_r"])
-
-
-def test_rht_and_inverse_match_reference():
-    from quant_2bit_b200.quant import apply_inverse_rht_gpu, apply_rht_gpu
-    d = _rht()
-    W = torch.tensor(d["W"])
-    sl, sr = torch.tensor(d["sign_l"]), torch.tensor(d["sign_r"])
-    Wt = apply_rht_gpu(W, sl, sr)
-    np.testing.assert_allclose(Wt.numpy(), d["W_rht"], rtol=1e-5, atol=1e-6)
-    np.testing.assert_allclose(apply_inverse_rht_gpu(torch.tensor(d["W_rht"]), sl, sr).numpy(),
-                               d["W_inv"], rtol=1e-5, atol=1e-6)
 
 
 def test_tile_order_matches_reference_and_round_trips():
@@ -93,12 +83,12 @@ def test_quantize_weight_matches_reference_pipeline(cuda_ok):
 
     Wr = torch.tensor(W, dtype=torch.float64, requires_grad=True)
     s_l, s_r = torch.tensor(sl, dtype=torch.float64), torch.tensor(sr, dtype=torch.float64)
-    Wt = quant.apply_rht_gpu(Wr, s_l, s_r)
+    Wt = torch_port.apply_rht(Wr, s_l, s_r)
     scale = Wt.detach().pow(2).mean().sqrt()
     seqs, info = quant._tile_for_viterbi_gpu(Wt / scale)
     soft, _ = torch_port.bcjr_forward_backward(seqs.reshape(seqs.shape[0], -1, V),
                                                torch.tensor(cb, dtype=torch.float64), T, L, k, V)
-    Wq_ref = quant.apply_inverse_rht_gpu(
+    Wq_ref = torch_port.apply_inverse_rht(
         quant._untile_from_viterbi_gpu(soft.reshape(seqs.shape), info, W.shape) * scale, s_l, s_r)
     (Wq_ref * torch.tensor(G, dtype=torch.float64)).sum().backward()
     np.testing.assert_allclose(Wq.detach().cpu().numpy(), Wq_ref.detach().numpy(),
