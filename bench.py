@@ -1,7 +1,7 @@
 """Benchmark: BCJR forward+backward state-transitions/sec on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c5|v2] [--temperature T] [--weights gauss|t3]
+                    [--config c2|c3|c5|v2|layer] [--temperature T] [--weights gauss|t3]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, NCCL)
 
 Workload (synthetic, seeded): L=16, k=2, V=1, N=256 steps,
@@ -17,6 +17,11 @@ T=0.5, codebook randn(65536) (seed 0), weights randn drawn after the codebook.
 * v2: the shape the reference's QAT layers use, k=2, V=2 (b = 4, 16
   predecessors per state), N=128: one 1024x1024 weight = 4,096 sequences of
   128 two-dimensional steps per GPU, codebook randn(65536, 2).
+* layer: the reference's QAT caller path on one Llama-3.2-1B decoder layer:
+  each of its 7 weights (per-row scale U[0.5, 2]) through
+  bcjr_quantize_weight (RHT, RMS scale, tile, BCJR at V=2, untile, inverse
+  RHT), forward and backward; 237,568 sequences of N=128.  Reports the time
+  of the RHT / tiling kernels as well.
 
 One step = forward (soft) + backward (d_seq for an upstream gradient of ones)
 of every local sequence (+ the all-gather when N > 1).  One transition = one
@@ -43,7 +48,7 @@ METRIC = "BCJR fwd+bwd state-transitions/sec (L=16,k=2) at 1/2/4/8 B200; % MUFU 
 UNIT = "transitions/s"
 L, K_BITS, TEMP = 16, 2, 0.5
 # (V, N) per config
-SHAPES = {"c2": (1, 256), "c3": (1, 256), "c5": (1, 256), "v2": (2, 128)}
+SHAPES = {"c2": (1, 256), "c3": (1, 256), "c5": (1, 256), "v2": (2, 128), "layer": (2, 128)}
 # Algorithmic MUFU (ex2/lg2/rcp) per state-step, forward call and backward
 # call: alpha LSE (2^b+1)/2^b + beta LSE (2^b+1)/2^b + marginal exp 1 for the
 # forward; the same recompute plus 2/2^b softmax normalisers for the
@@ -92,7 +97,7 @@ def make_inputs(config, rank, world, weights="gauss"):
             w = torch.tensor(np.random.default_rng(rank).standard_t(3, size=(4096, NSTEP, V))
                              / math.sqrt(3.0), dtype=torch.float32)
         return cb, w, 4096 * world
-    shapes = llama_layer_shapes() if config == "c3" else olmoe_layer_shapes()
+    shapes = llama_layer_shapes() if config in ("c3", "layer") else olmoe_layer_shapes()
     total = sum((m // 16) * (n // 16) for m, n in shapes)
     lo, hi = rank * total // world, (rank + 1) * total // world
     seqs, off = [], 0
@@ -101,7 +106,7 @@ def make_inputs(config, rank, world, weights="gauss"):
         cnt = (m // 16) * (n // 16)
         if off + cnt > lo and off < hi:
             gm = torch.Generator().manual_seed(100 + idx)
-            if config == "c3":
+            if config in ("c3", "layer"):
                 scale = torch.empty(m, 1).uniform_(0.5, 2.0, generator=gm)
             else:
                 scale = torch.empty(1, 1).uniform_(0.5, 2.0, generator=gm)
@@ -192,13 +197,136 @@ def cpu_reference(args, rank):
                       f"{threads} threads, {dt:.2f} s per step"}
 
 
+def hbm_peak_gbs():
+    """Measured copy bandwidth of this pool's B200s (MEASURED_PEAKS.json),
+    else the earlier measurement on this pool (6650 GB/s)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, "fallback"
+
+
+def run_layer(args, rank, world, local_rank):
+    """--config layer: bcjr_quantize_weight (RHT, RMS scale, tile, BCJR at V=2,
+    untile, inverse RHT), forward and backward, over the 7 weights of one
+    Llama-3.2-1B decoder layer; weights assigned round-robin to the ranks."""
+    from quant_2bit_b200 import quant
+    V, NSTEP = SHAPES["layer"]
+    edges_per_seq = NSTEP * (1 << L) * (1 << (K_BITS * V))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=600))
+    g = torch.Generator().manual_seed(0)
+    cb = torch.randn(1 << L, V, generator=g).to(dev)
+    T = torch.tensor(args.temperature, dtype=torch.float32, device=dev)
+    mats = []
+    for idx, (m, n) in enumerate(llama_layer_shapes()):
+        if idx % world != rank:
+            continue
+        gm = torch.Generator().manual_seed(100 + idx)
+        scale = torch.empty(m, 1).uniform_(0.5, 2.0, generator=gm)
+        W = (torch.randn(m, n, generator=gm) * scale).to(dev)
+        sl = torch.tensor(quant.make_sign_vector(m, 2 * idx), device=dev)
+        sr = torch.tensor(quant.make_sign_vector(n, 2 * idx + 1), device=dev)
+        mats.append((W, sl, sr, torch.ones(m, n, device=dev)))
+    seqs_local = sum(W.numel() // 256 for W, _, _, _ in mats)
+    seqs_total = sum(m * n // 256 for m, n in llama_layer_shapes())
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for W, sl, sr, ones in mats:
+            x = W.detach().requires_grad_(True)
+            quant.bcjr_quantize_weight(x, sl, sr, cb, T).backward(ones)
+
+    def wrapper_only():
+        for W, sl, sr, ones in mats:
+            x = W.detach().requires_grad_(True)
+            seqs, r = quant._RhtTile.apply(x, sl, sr)
+            quant._UntileIrht.apply(seqs, sl, sr, r, *W.shape).backward(ones)
+
+    def timed(fn, steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for e0, e1 in ev:
+            flush.zero_()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return sum(e0.elapsed_time(e1) for e0, e1 in ev)
+
+    for _ in range(args.warmup):
+        step()
+        wrapper_only()
+    torch.cuda.synchronize()
+    props = torch.cuda.get_device_properties(dev)
+    uuid = getattr(props, "uuid", None)
+    clocks = ClockSampler(f"GPU-{uuid}" if uuid is not None else local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    t_step = timed(step, args.steps)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    t_wrap = timed(wrapper_only, args.steps)
+    tt = torch.tensor([t_step, t_wrap], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        dist.destroy_process_group()
+    t_step, t_wrap = float(tt[0]), float(tt[1])
+    if rank != 0:
+        return
+    value = seqs_total * edges_per_seq * args.steps / (t_step / 1e3)
+    sms = props.multi_processor_count
+    clk_mhz = clk.get("sm_max_mhz") or 1965.0
+    peak = sms * MUFU_PER_SM_CLK * clk_mhz * 1e6 / 1e9
+    mufu_ops = sum(MUFU[V]) * seqs_total * NSTEP * (1 << L) / world
+    bcjr_ms = (t_step - t_wrap) / args.steps
+    elems = sum(W.numel() for W, _, _, _ in mats)
+    hbm, hbm_kind = hbm_peak_gbs()
+    wrap_bytes = 32.0 * elems          # read + write of every weight, 2 ops, fwd + bwd
+    wrap_gbs = wrap_bytes / (t_wrap / args.steps / 1e3) / 1e9
+    result = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_step / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded randn weights with per-row scale U[0.5, 2], randn codebook)",
+        "config": {"workload": "layer: bcjr_quantize_weight fwd+bwd over the 7 weights of one "
+                               f"Llama-3.2-1B layer (L=16, k=2, V=2, N=128, T={args.temperature:g})",
+                   "sequences_total": seqs_total, "sequences_per_gpu": seqs_local,
+                   "l2": "flushed between timed steps (256 MB write, outside the events)",
+                   "collective": "none (weights round-robin over ranks)"},
+        "clocks": clk,
+        # per weight: RHT+tile 5, BCJR forward 1, untile+inverse RHT 5; backward:
+        # tile 4, BCJR backward 1, untile+inverse RHT 5
+        "gpu_launches": 21 * len(mats) * args.steps,
+        "wrapper_ms": {"rht_tile_untile_irht_fwd_bwd": t_wrap / args.steps,
+                       "share_of_step": t_wrap / t_step},
+        "roofline": {"bound": "mufu", "kernel": "b4 forward + backward (step minus wrapper)",
+                     "achieved": mufu_ops / (bcjr_ms / 1e3) / 1e9, "peak": peak, "unit": "Gop/s",
+                     "frac": mufu_ops / (bcjr_ms / 1e3) / 1e9 / peak, "traffic": None},
+        "roofline_wrapper": {"bound": "hbm", "achieved": wrap_gbs, "peak": hbm, "unit": "GB/s",
+                             "frac": wrap_gbs / hbm, "peak_kind": hbm_kind,
+                             "note": "algorithmic bytes: each weight read and written once per op"},
+        "e2e": {"value": None, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(result), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5", "v2"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5", "v2", "layer"])
     ap.add_argument("--temperature", type=float, default=TEMP,
                     help="T (config 4 sweeps 4, 2, 1, 0.5, 0.25, 0.1, 0.05)")
     ap.add_argument("--weights", default="gauss", choices=["gauss", "t3"],
@@ -236,6 +364,10 @@ def main():
                 "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
+        return
+
+    if args.config == "layer":
+        run_layer(args, rank, world, local_rank)
         return
 
     import quant_2bit_b200 as q
