@@ -11,6 +11,10 @@ What is replaced (module attributes, looked up by the reference at call time):
   QuantizedLinear._compute_W_q (src/qat/quantized_linear.py:204-211) and so
   every QATDenseDecoderLayer projection -- goes through one launch of
   BcjrForwardBackwardMonolithic;
+* src.bcjr.bcjr_quant.bcjr_quantize_weight and the name
+  src.qat.quantized_linear imported from it (src/bcjr/bcjr_quant.py:159-178,
+  src/qat/quantized_linear.py:41): RHT, RMS scale and tiling on both sides
+  of the op run as native kernels;
 * src.bcjr.bcjr_monolithic.BcjrForwardBackwardMonolithic and
   bcjr_forward_backward_monolithic (src/bcjr/bcjr_monolithic.py:157-262);
 * src.bcjr.bcjr_quant.apply_rht_gpu / apply_inverse_rht_gpu and the same
@@ -44,6 +48,12 @@ def install(patch_rht=None):
     ste = importlib.import_module("src.qat.ste")
     _patch(bq, "_bcjr_chunk_forward", _quant._bcjr_chunk_forward)
     _patch(bq, "bcjr_quantize_tiles", _quant.bcjr_quantize_tiles)
+    _patch(bq, "bcjr_quantize_weight", _quant.bcjr_quantize_weight)
+    try:
+        ql = importlib.import_module("src.qat.quantized_linear")
+        _patch(ql, "bcjr_quantize_weight", _quant.bcjr_quantize_weight)
+    except Exception:       # optional: its imports may need packages not present
+        pass
     if bm is not None:
         _patch(bm, "BcjrForwardBackwardMonolithic", _bcjr.BcjrForwardBackwardMonolithic)
         _patch(bm, "bcjr_forward_backward_monolithic", _bcjr.bcjr_forward_backward_monolithic)

@@ -52,7 +52,9 @@ def test_hook_patches_reference_modules():
     try:
         names = hook.install()
         assert "src.bcjr.bcjr_quant._bcjr_chunk_forward" in names
+        assert "src.bcjr.bcjr_quant.bcjr_quantize_weight" in names
         assert bq._bcjr_chunk_forward is quant._bcjr_chunk_forward
+        assert bq.bcjr_quantize_weight is quant.bcjr_quantize_weight
         assert bq.bcjr_quantize_tiles is quant.bcjr_quantize_tiles
         if not getattr(ste, "_HAS_FHT", False):
             assert bq.apply_rht_gpu is quant.apply_rht_gpu
