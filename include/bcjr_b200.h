@@ -188,6 +188,27 @@ BCJR_API int bcjr_untile_irht(const float *seqs, const float *sign_l, const floa
                               int n, const float *s_dev, float *out, void *ws, size_t ws_bytes,
                               bcjr_stream_t stream);
 
+/*
+ * Hard (min-sum) Viterbi encoding of B sequences of N steps (seq: B x N x V
+ * fp32, i.e. the reference's (B, T) with T = N V) over the same trellis and
+ * codebook.  Outputs: bitstreams (B x N int32, the low kV bits of each state
+ * of the best walk), start_states (B int32, the state before step 0),
+ * recons (B x N x V fp32, the walk's codewords) and mses (B fp32, mean
+ * squared error of recons).  Replaces viterbi_encode_v_batched_cuda
+ * (src/viterbi/cuda_kernel.py:147-220, L=16, k=2, V=2 only) and the numpy
+ * encoders viterbi_encode_v / viterbi_encode_v_batched
+ * (src/viterbi/encode.py:258-310, :425-497): costs accumulate as in
+ * viterbi_encode_v (fp32, d = c - w, d*d summed over V, no fused
+ * multiply-add), ties go to the lowest predecessor index and the lowest
+ * final state, so walks are bit-identical to it.  Shapes as for the BCJR
+ * op; workspace of bcjr_viterbi_workspace_bytes bytes, 256-byte aligned
+ * (fewer bytes run fewer sequences at a time).
+ */
+BCJR_API size_t bcjr_viterbi_workspace_bytes(int B, int N, int L, int k, int V);
+BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L, int k, int V,
+                          int *bitstreams, int *start_states, float *recons, float *mses,
+                          void *ws, size_t ws_bytes, bcjr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

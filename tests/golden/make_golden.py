@@ -11,7 +11,7 @@ Input generation follows the benchmark configs: torch.Generator seeded with
 ``seed``; the codebook is drawn first, then the weights; Student-t weights use
 numpy.random.default_rng(seed).standard_t(3) / sqrt(3).
 
-    python tests/golden/make_golden.py --ref <reference root> [--only c1|small|l16|v2|v2sweep|rht]
+    python tests/golden/make_golden.py --ref <reference root> [--only c1|small|l16|v2|v2sweep|rht|viterbi]
 """
 import argparse
 import math
@@ -129,6 +129,38 @@ def gen_v2sweep(ref_fb, ref_root):
          cb_rows=rows, cb_at_rows=cb_hyb[rows], **out)
 
 
+def gen_viterbi(ref_root):
+    # Hard Viterbi encodes of the reference's exact-arithmetic encoders
+    # (src/viterbi/encode.py:47-90 viterbi_encode, :258-310 viterbi_encode_v),
+    # one fixture per trellis: (L, k, V, sequences, steps, codebook kind).
+    from src.viterbi.encode import viterbi_encode, viterbi_encode_v
+    from src.codes.ref import decode_hyb_batch
+    cases = [(16, 2, 2, 4, 128, "hyb"), (16, 2, 2, 3, 128, "gauss"), (16, 2, 1, 3, 256, "gauss"),
+             (8, 2, 1, 4, 64, "gauss"), (10, 2, 2, 4, 32, "gauss"), (9, 3, 1, 3, 40, "gauss"),
+             (6, 1, 1, 4, 50, "gauss")]
+    for (L, k, V, B, N, kind) in cases:
+        rng = np.random.default_rng(1000 + 10 * L + V)
+        if kind == "hyb":
+            lut = rng.standard_normal((512, 2)).astype(np.float32)
+            cb = decode_hyb_batch(np.arange(1 << L, dtype=np.uint32), lut, Q=9).astype(np.float32)
+        else:
+            cb = rng.standard_normal((1 << L, V)).astype(np.float32)
+        seqs = rng.standard_normal((B, N * V)).astype(np.float32)
+        out = {"bits": [], "starts": [], "recons": [], "mses": []}
+        for i in range(B):
+            if V == 1:
+                bs, ss, rec, mse = viterbi_encode(seqs[i], L=L, k=k, decode_fn=lambda st: cb[st, 0])
+            else:
+                bs, ss, rec, mse = viterbi_encode_v(seqs[i], L=L, k=k, V=V, decode_fn=lambda st: cb[st])
+            out["bits"].append(bs); out["starts"].append(ss)
+            out["recons"].append(rec); out["mses"].append(mse)
+        extra = {"lut": lut} if kind == "hyb" else {"cb": cb}
+        save(f"viterbi_L{L}_k{k}_V{V}_{kind}.npz", seqs=seqs, L=L, k=k, V=V,
+             bits=np.array(out["bits"], np.int32), starts=np.array(out["starts"], np.int32),
+             recons=np.array(out["recons"], np.float32), mses=np.array(out["mses"], np.float32),
+             **extra)
+
+
 def gen_rht(ref_root):
     # RHT, sign vectors and tile order of the reference's quantizer wrapper
     # (src/rht/transform.py:59-126, src/qat/ste.py:76-110).
@@ -152,10 +184,12 @@ def main():
     sys.path.insert(0, args.ref)
     from src.bcjr.forward_backward import bcjr_forward_backward as ref_fb
     torch.set_num_threads(os.cpu_count() or 1)
-    todo = [args.only] if args.only else ["small", "c1", "v2", "l16", "v2sweep", "rht"]
+    todo = [args.only] if args.only else ["small", "c1", "v2", "l16", "v2sweep", "rht", "viterbi"]
     for what in todo:
         if what == "rht":
             gen_rht(args.ref)
+        elif what == "viterbi":
+            gen_viterbi(args.ref)
         elif what == "v2sweep":
             gen_v2sweep(ref_fb, args.ref)
         else:

@@ -1,0 +1,95 @@
+"""Hard Viterbi encoder: the CPU oracle (oracle/viterbi.py) against the
+reference's own encodes (tests/golden/viterbi_*.npz, made by running
+src/viterbi/encode.py), and (GPU) the sm_100a kernel against both, bit-exact
+on walks, bitstreams, start states and reconstructions."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_names, hyb_codebook, load_golden
+from oracle import viterbi
+
+NAMES = golden_names("viterbi_*.npz")
+
+
+def _case(name):
+    d = load_golden(name)
+    return d, d["cb"].reshape(1 << d["L"], d["V"])
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_oracle_matches_reference_encoder(name):
+    d, cb = _case(name)
+    bits, starts, rec, mse = viterbi.viterbi(d["seqs"], cb, d["L"], d["k"], d["V"])
+    np.testing.assert_array_equal(bits, d["bits"])
+    np.testing.assert_array_equal(starts, d["starts"])
+    np.testing.assert_array_equal(rec, d["recons"])
+    np.testing.assert_allclose(mse, d["mses"], rtol=1e-6, atol=1e-7)
+
+
+def test_oracle_walk_replays_to_its_reconstruction():
+    """viterbi_decode (src/viterbi/encode.py:313-328): replaying the bitstream
+    from the start state gives the reconstruction."""
+    rng = np.random.default_rng(3)
+    L, k, V = 8, 2, 2
+    cb = rng.standard_normal((1 << L, V)).astype(np.float32)
+    seqs = rng.standard_normal((3, 40)).astype(np.float32)
+    bits, starts, rec, _ = viterbi.viterbi(seqs, cb, L, k, V)
+    for i in range(3):
+        s = int(starts[i])
+        out = []
+        for t in range(bits.shape[1]):
+            s = ((s << (k * V)) | int(bits[i, t])) & ((1 << L) - 1)
+            out.append(cb[s])
+        np.testing.assert_array_equal(np.concatenate(out), rec[i])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", NAMES)
+def test_kernel_matches_reference_encoder(cuda_ok, name):
+    from quant_2bit_b200.viterbi import viterbi_encode_batched
+    d, cb = _case(name)
+    out = viterbi_encode_batched(torch.tensor(d["seqs"], device="cuda"),
+                                 torch.tensor(cb, device="cuda"), d["L"], d["k"], d["V"])
+    bits, starts, rec, mse = [o.cpu().numpy() for o in out]
+    np.testing.assert_array_equal(bits, d["bits"])
+    np.testing.assert_array_equal(starts, d["starts"])
+    np.testing.assert_array_equal(rec, d["recons"])
+    np.testing.assert_allclose(mse, d["mses"], rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("L,k,V,B,N,kind", [(16, 2, 2, 301, 128, "hyb"), (16, 2, 1, 5, 256, "gauss"),
+                                            (16, 2, 2, 2, 1, "gauss"), (12, 1, 2, 7, 33, "gauss"),
+                                            (4, 2, 2, 3, 9, "gauss"), (16, 4, 1, 2, 64, "gauss")])
+def test_kernel_matches_oracle(cuda_ok, L, k, V, B, N, kind):
+    """Ragged and large batches (more sequences than blocks), N = 1, the
+    smallest trellis, and a HYB codebook (repeated codewords: exact ties,
+    resolved to the lowest index as in the reference)."""
+    from quant_2bit_b200.viterbi import viterbi_encode_batched
+    rng = np.random.default_rng(L * 100 + B)
+    cb = (hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32)) if kind == "hyb"
+          else rng.standard_normal((1 << L, V)).astype(np.float32))
+    seqs = rng.standard_normal((B, N * V)).astype(np.float32)
+    out = viterbi_encode_batched(torch.tensor(seqs, device="cuda"), torch.tensor(cb, device="cuda"),
+                                 L, k, V)
+    bits, starts, rec, mse = [o.cpu().numpy() for o in out]
+    rb, rs, rr, rm = viterbi.viterbi(seqs, cb, L, k, V)
+    np.testing.assert_array_equal(bits, rb)
+    np.testing.assert_array_equal(starts, rs)
+    np.testing.assert_array_equal(rec, rr)
+    np.testing.assert_allclose(mse, rm, rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.gpu
+def test_reference_entry_point_and_errors(cuda_ok):
+    from quant_2bit_b200.viterbi import viterbi_encode_v_batched_cuda
+    d, cb = _case("viterbi_L16_k2_V2_gauss.npz")
+    bits, starts, rec, mse = viterbi_encode_v_batched_cuda(torch.tensor(d["seqs"], device="cuda"),
+                                                           torch.tensor(cb, device="cuda"))
+    np.testing.assert_array_equal(bits.cpu().numpy(), d["bits"])
+    with pytest.raises(RuntimeError):
+        viterbi_encode_v_batched_cuda(torch.zeros(2, 8), torch.zeros(16, 2))
+    with pytest.raises(AssertionError):
+        viterbi_encode_v_batched_cuda(torch.zeros(2, 7, device="cuda"),
+                                      torch.zeros(16, 2, device="cuda"))
