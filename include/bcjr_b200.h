@@ -202,7 +202,10 @@ BCJR_API int bcjr_untile_irht(const float *seqs, const float *sign_l, const floa
  * multiply-add), ties go to the lowest predecessor index and the lowest
  * final state, so walks are bit-identical to it.  Shapes as for the BCJR
  * op; workspace of bcjr_viterbi_workspace_bytes bytes, 256-byte aligned
- * (fewer bytes run fewer sequences at a time).
+ * (L=16, k=2, V=2 runs on 4-CTA clusters and needs N * 4096 bytes per
+ * sequence for up to 2048 sequences at a time; other shapes run fewer
+ * sequences at a time when given fewer bytes).  bcjr_ws_status reports a
+ * device-side wait timeout.
  */
 BCJR_API size_t bcjr_viterbi_workspace_bytes(int B, int N, int L, int k, int V);
 BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L, int k, int V,

@@ -43,4 +43,11 @@ int b4_clusters(int B, int mode);
 size_t b4_workspace_bytes(int B, int N, int mode);
 cudaError_t launch_b4(const LaunchArgs &a);
 
+// Cluster Viterbi for L=16, k=2, V=2, 1 <= N <= 512 (bcjr_vit_b4.cu).
+bool vit_b4_applicable(int N, int L, int k, int V, const void *cb);
+size_t vit_b4_workspace_bytes(int B, int N);
+cudaError_t launch_vit_b4(const float *seq, const float *cb, int B, int N, int *bits,
+                          int *starts, float *recon, float *mse, void *ws, size_t ws_bytes,
+                          int *status, cudaStream_t st);
+
 }  // namespace bcjr

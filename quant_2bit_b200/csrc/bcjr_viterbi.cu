@@ -21,6 +21,7 @@
 // to the same slot, and thread 0 walks back at the end.
 #include <cfloat>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 
 #include "../../include/bcjr_b200.h"
@@ -194,12 +195,28 @@ cudaError_t vit_launch(const float *seq, const float *cb, int B, int N, int L, u
 
 extern "C" {
 
+// Workspace: a 256-byte header (device status word, read by bcjr_ws_status)
+// then the kernel's data: the cluster kernel's backpointers for L=16, k=2,
+// V=2 (bcjr_vit_b4.cu), else sequence slots of the generic kernel.
+constexpr size_t kVitHeader = 256;
+
+bool vit_use_cluster(int N, int L, int k, int V, const void *cb) {
+    const char *env = std::getenv("BCJR_B200_FORCE_GENERIC");
+    if (env && env[0] == '1') return false;
+    return bcjr::vit_b4_applicable(N, L, k, V, cb);
+}
+
 BCJR_API size_t bcjr_viterbi_workspace_bytes(int B, int N, int L, int k, int V) {
     if (vit_check(B, N, L, k, V)) return 0;
     const int cap = vit_grid_cap();
     if (cap <= 0) return 0;
     const long grid = B < cap ? (B > 0 ? B : 1) : cap;
-    return (size_t)grid * bcjr::vit::slot_bytes(N, L, k * V);
+    size_t need = (size_t)grid * bcjr::vit::slot_bytes(N, L, k * V);
+    if (vit_use_cluster(N, L, k, V, nullptr)) {
+        const size_t c = bcjr::vit_b4_workspace_bytes(B, N);
+        if (c > need) need = c;
+    }
+    return kVitHeader + need;
 }
 
 BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L, int k, int V,
@@ -215,19 +232,29 @@ BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L
          reinterpret_cast<uintptr_t>(recons) | reinterpret_cast<uintptr_t>(mses)) & 3u)
         return BCJR_ERR_ALIGNMENT;
     if (reinterpret_cast<uintptr_t>(ws) & 255u) return BCJR_ERR_ALIGNMENT;
+    if (ws_bytes <= kVitHeader) return BCJR_ERR_WORKSPACE;
     int dev = 0, major = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
         major != 10)
         return BCJR_ERR_DEVICE;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int *status = static_cast<int *>(ws);
+    void *data = static_cast<char *>(ws) + kVitHeader;
+    const size_t data_bytes = ws_bytes - kVitHeader;
+    if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return BCJR_ERR_LAUNCH;
+    if (vit_use_cluster(N, L, k, V, cb) && data_bytes >= bcjr::vit_b4_workspace_bytes(B, N)) {
+        const cudaError_t e = bcjr::launch_vit_b4(seq, cb, B, N, bitstreams, start_states, recons,
+                                                  mses, data, data_bytes, status, s);
+        return e == cudaSuccess ? BCJR_OK : BCJR_ERR_LAUNCH;
+    }
     const size_t slot = bcjr::vit::slot_bytes(N, L, k * V);
-    long grid = (long)(ws_bytes / slot);
+    long grid = (long)(data_bytes / slot);
     if (grid > B) grid = B;
     const int cap = vit_grid_cap();
     if (cap > 0 && grid > cap) grid = cap;
     if (grid < 1) return BCJR_ERR_WORKSPACE;
-    unsigned char *w = static_cast<unsigned char *>(ws);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char *w = static_cast<unsigned char *>(data);
     cudaError_t e;
     switch (k * V * 10 + V) {
         case 11: e = vit_launch<1, 1>(seq, cb, B, N, L, w, slot, (int)grid, bitstreams, start_states, recons, mses, s); break;

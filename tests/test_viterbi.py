@@ -93,3 +93,26 @@ def test_reference_entry_point_and_errors(cuda_ok):
     with pytest.raises(AssertionError):
         viterbi_encode_v_batched_cuda(torch.zeros(2, 7, device="cuda"),
                                       torch.zeros(16, 2, device="cuda"))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,N", [(64, 128), (2049, 8), (3, 512)])
+def test_cluster_and_generic_kernels_agree(cuda_ok, B, N):
+    """L=16, k=2, V=2 runs on the 4-CTA cluster kernel; BCJR_B200_FORCE_GENERIC=1
+    sends it to the one-block-per-sequence kernel.  Both are exact: identical
+    results, across the 2048-sequence chunking of the cluster path and at the
+    longest N it serves."""
+    import os
+    from quant_2bit_b200.viterbi import viterbi_encode_batched
+    rng = np.random.default_rng(B + N)
+    cb = torch.tensor(hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32)), device="cuda")
+    seqs = torch.tensor(rng.standard_normal((B, 2 * N)).astype(np.float32), device="cuda")
+    a = viterbi_encode_batched(seqs, cb, 16, 2, 2)
+    os.environ["BCJR_B200_FORCE_GENERIC"] = "1"
+    try:
+        b = viterbi_encode_batched(seqs, cb, 16, 2, 2)
+    finally:
+        del os.environ["BCJR_B200_FORCE_GENERIC"]
+    for x, y in zip(a[:3], b[:3]):
+        assert torch.equal(x, y)
+    torch.testing.assert_close(a[3], b[3], rtol=1e-6, atol=1e-7)
