@@ -1,7 +1,7 @@
 """Benchmark: BCJR forward+backward state-transitions/sec on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c5|v2|layer] [--temperature T] [--weights gauss|t3]
+                    [--config c2|c3|c5|v2|layer|viterbi] [--temperature T] [--weights gauss|t3]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, NCCL)
 
 Workload (synthetic, seeded): L=16, k=2, V=1, N=256 steps,
@@ -22,6 +22,9 @@ T=0.5, codebook randn(65536) (seed 0), weights randn drawn after the codebook.
   bcjr_quantize_weight (RHT, RMS scale, tile, BCJR at V=2, untile, inverse
   RHT), forward and backward; 237,568 sequences of N=128.  Reports the time
   of the RHT / tiling kernels as well.
+* viterbi: hard (min-sum) Viterbi encoding of config v2's sequences (one
+  1024x1024 weight per GPU at L=16, k=2, V=2), the reference's
+  viterbi_encode_v_batched_cuda; its own metric (min-sum transitions/s).
 
 One step = forward (soft) + backward (d_seq for an upstream gradient of ones)
 of every local sequence (+ the all-gather when N > 1).  One transition = one
@@ -48,7 +51,9 @@ METRIC = "BCJR fwd+bwd state-transitions/sec (L=16,k=2) at 1/2/4/8 B200; % MUFU 
 UNIT = "transitions/s"
 L, K_BITS, TEMP = 16, 2, 0.5
 # (V, N) per config
-SHAPES = {"c2": (1, 256), "c3": (1, 256), "c5": (1, 256), "v2": (2, 128), "layer": (2, 128)}
+SHAPES = {"c2": (1, 256), "c3": (1, 256), "c5": (1, 256), "v2": (2, 128), "layer": (2, 128),
+          "viterbi": (2, 128)}
+VITERBI_METRIC = "Viterbi (min-sum) state-transitions/sec (L=16,k=2,V=2), 1 B200"
 # Algorithmic MUFU (ex2/lg2/rcp) per state-step, forward call and backward
 # call: alpha LSE (2^b+1)/2^b + beta LSE (2^b+1)/2^b + marginal exp 1 for the
 # forward; the same recompute plus 2/2^b softmax normalisers for the
@@ -90,7 +95,7 @@ def make_inputs(config, rank, world, weights="gauss"):
     V, NSTEP = SHAPES[config]
     g = torch.Generator().manual_seed(0)
     cb = torch.randn(1 << L, V, generator=g)
-    if config in ("c2", "v2"):
+    if config in ("c2", "v2", "viterbi"):
         gw = torch.Generator().manual_seed(1000 + rank) if rank else g
         w = torch.randn(4096, NSTEP, V, generator=gw)
         if weights == "t3":
@@ -175,6 +180,8 @@ def cpu_reference(args, rank):
     """The reference's eager torch BCJR (restated in oracle/torch_port.py) on
     the host's CPU cores: one forward + backward of a bounded sample of the
     same workload per step."""
+    if args.config == "viterbi":
+        return cpu_viterbi(args)
     from oracle import torch_port
     V, NSTEP = SHAPES[args.config]
     edges_per_seq = NSTEP * (1 << L) * (1 << (K_BITS * V))
@@ -320,13 +327,135 @@ def run_layer(args, rank, world, local_rank):
     print(json.dumps(result), flush=True)
 
 
+def cpu_viterbi(args):
+    """The reference's exact-arithmetic Viterbi encoder (viterbi_encode_v,
+    restated vectorised in oracle/viterbi.py) on the host cores, on a bounded
+    sample of config viterbi's sequences."""
+    from oracle import viterbi as ov
+    V, NSTEP = SHAPES["viterbi"]
+    cb, w, _ = make_inputs("viterbi", 0, 1)
+    nseq = max(args.cpu_sample_seqs, 4)
+    sample = w[:nseq].reshape(nseq, NSTEP * V).numpy()
+    cbn = cb.numpy()
+    for _ in range(args.warmup if args.impl == "reference" else 0):
+        ov.viterbi(sample, cbn, L, K_BITS, V)
+    steps = args.steps if args.impl == "reference" else 1
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ov.viterbi(sample, cbn, L, K_BITS, V)
+    dt = (time.perf_counter() - t0) / steps
+    value = nseq * NSTEP * (1 << L) * (1 << (K_BITS * V)) / dt
+    return {"value": value, "unit": UNIT, "cores": 1, "kind": "port", "sample_sequences": nseq,
+            "sample": f"{nseq} sequences of config viterbi (L=16, V=2, N=128), numpy "
+                      f"{np.__version__} (one thread of vector work), {dt:.2f} s per step"}
+
+
+def run_viterbi(args, rank, world, local_rank):
+    """--config viterbi: one 1024x1024 weight per GPU as 4096 sequences of 128
+    two-dimensional steps, hard Viterbi encoded (bitstreams, start states,
+    reconstructions, MSEs)."""
+    from quant_2bit_b200.viterbi import viterbi_encode_batched
+    V, NSTEP = SHAPES["viterbi"]
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    cb_cpu, w_cpu, _ = make_inputs("viterbi", rank, world)
+    if args.sequences:
+        w_cpu = w_cpu[:args.sequences]
+    Bl = w_cpu.shape[0]
+    seqs_cpu = w_cpu.reshape(Bl, NSTEP * V).contiguous()
+    cb = cb_cpu.to(dev)
+    seqs = seqs_cpu.to(dev)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        viterbi_encode_batched(seqs, cb, L, K_BITS, V)
+    torch.cuda.synchronize()
+    props = torch.cuda.get_device_properties(dev)
+    uuid = getattr(props, "uuid", None)
+    clocks = ClockSampler(f"GPU-{uuid}" if uuid is not None else local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record(stream)
+        viterbi_encode_batched(seqs, cb, L, K_BITS, V)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    t_ms = sum(e0.elapsed_time(e1) for e0, e1 in ev)
+    # e2e: pinned host sequences in, bitstreams and reconstructions out
+    host_in = seqs_cpu.pin_memory()
+    bits_h = torch.empty((Bl, NSTEP), dtype=torch.int32).pin_memory()
+    rec_h = torch.empty((Bl, NSTEP * V)).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        b, st, rec, mse = viterbi_encode_batched(host_in.to(dev, non_blocking=True), cb, L, K_BITS, V)
+        bits_h.copy_(b, non_blocking=True)
+        rec_h.copy_(rec, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_e2e = e0.elapsed_time(e1)
+    tt = torch.tensor([t_ms, t_e2e], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    t_ms, t_e2e = float(tt[0]), float(tt[1])
+    per_seq = NSTEP * (1 << L) * (1 << (K_BITS * V))
+    value = Bl * world * per_seq * args.steps / (t_ms / 1e3)
+    # issue roofline: per state-step the exact min-sum needs d = c - w and its
+    # square for 2 dimensions, their sum, the add of the group minimum (3 f32x2
+    # instructions per 2 states = 3 per state) and a compare / select for the
+    # minimum and its index (2 per state): 5 thread instructions; peak 128
+    # thread instructions per clock per SM
+    sms = props.multi_processor_count
+    clk_mhz = clk.get("sm_max_mhz") or 1965.0
+    ops = 5.0 * Bl * NSTEP * (1 << L) * args.steps
+    achieved = ops / (t_ms / 1e3) / 1e9
+    peak = sms * 128 * clk_mhz * 1e6 / 1e9
+    result = {
+        "metric": VITERBI_METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded randn codebook (65536, 2) and weights)",
+        "config": {"workload": "viterbi: one 1024x1024 weight per GPU, 4096 sequences of "
+                               "N=128 at L=16, k=2, V=2 (bitstreams, starts, recons, MSEs)",
+                   "sequences_per_gpu": Bl, "sequences_total": Bl * world,
+                   "l2": "flushed between timed steps (256 MB write, outside the events)"},
+        "clocks": clk,
+        "gpu_launches": 2 * args.steps,
+        "roofline": {"bound": "issue", "kernel": "vit_b4_kernel + walk-back",
+                     "achieved": achieved, "peak": peak, "unit": "Ginst/s", "frac": achieved / peak,
+                     "traffic": float(Bl * NSTEP * 4096),
+                     "traffic_unit": "backpointer bytes written per launch",
+                     "note": "5 algorithmic thread instructions per state-step; "
+                             f"peak {sms} SMs x 128/clk x {clk_mhz:.0f} MHz"},
+        "e2e": {"value": Bl * world * per_seq * args.steps / (t_e2e / 1e3), "unit": UNIT,
+                "h2d_bytes_per_step": host_in.numel() * 4,
+                "d2h_bytes_per_step": (bits_h.numel() + rec_h.numel()) * 4},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_viterbi(args)
+    print(json.dumps(result), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5", "v2", "layer"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5", "v2", "layer", "viterbi"])
     ap.add_argument("--temperature", type=float, default=TEMP,
                     help="T (config 4 sweeps 4, 2, 1, 0.5, 0.25, 0.1, 0.05)")
     ap.add_argument("--weights", default="gauss", choices=["gauss", "t3"],
@@ -351,15 +480,17 @@ def main():
         if rank != 0:
             return
         ref = cpu_reference(args, rank)
-        line = {"metric": METRIC, "value": ref["value"], "unit": UNIT, "n_gpus": args.gpus,
+        nsample = ref.get("sample_sequences", args.cpu_sample_seqs)
+        line = {"metric": VITERBI_METRIC if args.config == "viterbi" else METRIC,
+                "value": ref["value"], "unit": UNIT, "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": args.cpu_sample_seqs * EDGES_PER_SEQ / ref["value"] * 1e3,
+                "ms_per_step": nsample * EDGES_PER_SEQ / ref["value"] * 1e3,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic (seeded randn, BASELINE configs)",
                 "impl": "reference",
                 "config": {"workload": f"{args.config}: L=16 k=2 V={V} N={NSTEP} T={args.temperature:g} "
                                        f"{args.weights} weights, CPU sample",
-                           "sample_sequences": args.cpu_sample_seqs},
+                           "sample_sequences": nsample},
                 "cpu_baseline": ref,
                 "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
@@ -368,6 +499,9 @@ def main():
 
     if args.config == "layer":
         run_layer(args, rank, world, local_rank)
+        return
+    if args.config == "viterbi":
+        run_viterbi(args, rank, world, local_rank)
         return
 
     import quant_2bit_b200 as q
