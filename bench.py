@@ -245,6 +245,12 @@ def run_layer(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
 
     def step():
+        # the whole layer: one BCJR launch per direction for all weights' tiles
+        xs = [W.detach().requires_grad_(True) for W, _, _, _ in mats]
+        outs = quant.bcjr_quantize_layer(xs, [m[1] for m in mats], [m[2] for m in mats], cb, T)
+        torch.autograd.backward(outs, [m[3] for m in mats])
+
+    def step_per_weight():
         for W, sl, sr, ones in mats:
             x = W.detach().requires_grad_(True)
             quant.bcjr_quantize_weight(x, sl, sr, cb, T).backward(ones)
@@ -282,12 +288,13 @@ def run_layer(args, rank, world, local_rank):
         dist.barrier()
     clk = clocks.stop()
     t_wrap = timed(wrapper_only, args.steps)
-    tt = torch.tensor([t_step, t_wrap], dtype=torch.float64, device=dev)
+    t_pw = timed(step_per_weight, args.steps)
+    tt = torch.tensor([t_step, t_wrap, t_pw], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         dist.barrier()
         dist.destroy_process_group()
-    t_step, t_wrap = float(tt[0]), float(tt[1])
+    t_step, t_wrap, t_pw = float(tt[0]), float(tt[1]), float(tt[2])
     if rank != 0:
         return
     value = seqs_total * edges_per_seq * args.steps / (t_step / 1e3)
@@ -305,17 +312,19 @@ def run_layer(args, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": t_step / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded randn weights with per-row scale U[0.5, 2], randn codebook)",
-        "config": {"workload": "layer: bcjr_quantize_weight fwd+bwd over the 7 weights of one "
-                               f"Llama-3.2-1B layer (L=16, k=2, V=2, N=128, T={args.temperature:g})",
+        "config": {"workload": "layer: bcjr_quantize_layer fwd+bwd over the 7 weights of one "
+                               f"Llama-3.2-1B layer (L=16, k=2, V=2, N=128, T={args.temperature:g}), "
+                               "one BCJR launch per direction",
                    "sequences_total": seqs_total, "sequences_per_gpu": seqs_local,
                    "l2": "flushed between timed steps (256 MB write, outside the events)",
                    "collective": "none (weights round-robin over ranks)"},
         "clocks": clk,
-        # per weight: RHT+tile 5, BCJR forward 1, untile+inverse RHT 5; backward:
-        # tile 4, BCJR backward 1, untile+inverse RHT 5
-        "gpu_launches": 21 * len(mats) * args.steps,
+        # per weight: RHT+tile 5, untile+inverse RHT 5; backward: tile 4,
+        # untile+inverse RHT 5; plus one BCJR forward and one backward
+        "gpu_launches": (19 * len(mats) + 2) * args.steps,
         "wrapper_ms": {"rht_tile_untile_irht_fwd_bwd": t_wrap / args.steps,
                        "share_of_step": t_wrap / t_step},
+        "per_weight_ms_per_step": t_pw / args.steps,
         "roofline": {"bound": "mufu", "kernel": "b4 forward + backward (step minus wrapper)",
                      "achieved": mufu_ops / (bcjr_ms / 1e3) / 1e9, "peak": peak, "unit": "Gop/s",
                      "frac": mufu_ops / (bcjr_ms / 1e3) / 1e9 / peak, "traffic": None},

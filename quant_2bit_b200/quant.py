@@ -236,9 +236,40 @@ def bcjr_quantize_weight(W_latent, sign_l, sign_r, codebook, T_temp, preds=None,
     return _UntileIrht.apply(soft.reshape(B, TX * TY), sign_l, sign_r, rms, m, n)
 
 
+def bcjr_quantize_layer(weights, signs_l, signs_r, codebook, T_temp, preds=None, succs=None):
+    """bcjr_quantize_weight for several weights at once (e.g. the 7 projections
+    of a decoder layer, or the experts of an MoE layer), with one BCJR launch
+    per direction for all their tiles: each weight is rotated, scaled and
+    tiled by itself (its own RMS scale and sign vectors, as
+    bcjr_quantize_weight does), the tiles of all weights go through the op
+    together, and each weight is untiled and rotated back.  Returns the list
+    of quantized weights; gradients flow to every weight."""
+    assert len(weights) == len(signs_l) == len(signs_r)
+    if preds is None or succs is None:
+        L = int(round(math.log2(codebook.shape[0])))
+        preds, succs = build_pred_succ_tables(L=L, k=K_BITS, V=codebook.shape[1],
+                                              device=weights[0].device)
+    V = codebook.shape[1]
+    tiles, scales, counts = [], [], []
+    for W, sl, sr in zip(weights, signs_l, signs_r):
+        seqs, rms = _RhtTile.apply(W, sl, sr)
+        tiles.append(seqs)
+        scales.append(rms)
+        counts.append(seqs.shape[0])
+    allseq = torch.cat(tiles, dim=0)
+    Bt = allseq.shape[0]
+    soft = bcjr_quantize_tiles(allseq.view(Bt, (TX * TY) // V, V), codebook, T_temp, preds, succs)
+    out = []
+    for part, W, sl, sr, rms in zip(torch.split(soft.reshape(Bt, TX * TY), counts, dim=0), weights,
+                                    signs_l, signs_r, scales):
+        m, n = W.shape
+        out.append(_UntileIrht.apply(part, sl, sr, rms, m, n))
+    return out
+
+
 __all__ = [
     "TX", "TY", "BCJR_CHUNK", "L_BITS", "K_BITS", "V_DIM", "make_sign_vector",
     "apply_rht_gpu", "apply_inverse_rht_gpu", "_tile_for_viterbi_gpu",
     "_untile_from_viterbi_gpu", "_bcjr_chunk_forward", "bcjr_quantize_tiles",
-    "bcjr_quantize_weight_rotated", "bcjr_quantize_weight",
+    "bcjr_quantize_weight_rotated", "bcjr_quantize_weight", "bcjr_quantize_layer",
 ]

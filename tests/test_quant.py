@@ -96,3 +96,28 @@ def test_quantize_weight_matches_reference_pipeline(cuda_ok):
     np.testing.assert_allclose(Wq.detach().cpu().numpy(), Wq_ref.detach().numpy(),
                                rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(Wd.grad.cpu().numpy(), Wr.grad.numpy(), rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.gpu
+def test_quantize_layer_equals_per_weight(cuda_ok):
+    """bcjr_quantize_layer (all weights' tiles in one BCJR launch per direction)
+    gives bitwise the results and gradients of bcjr_quantize_weight per weight:
+    per-sequence results do not depend on the batch."""
+    from quant_2bit_b200 import quant
+    rng = np.random.default_rng(8)
+    cb = torch.tensor(rng.standard_normal((65536, 2)).astype(np.float32), device="cuda")
+    T = torch.tensor(0.4, device="cuda")
+    shapes = [(64, 32), (16, 128), (32, 32)]
+    Ws = [torch.tensor(rng.standard_normal(s).astype(np.float32), device="cuda") for s in shapes]
+    sls = [torch.tensor(quant.make_sign_vector(m, 10 + i), device="cuda") for i, (m, n) in enumerate(shapes)]
+    srs = [torch.tensor(quant.make_sign_vector(n, 20 + i), device="cuda") for i, (m, n) in enumerate(shapes)]
+    Gs = [torch.tensor(rng.standard_normal(s).astype(np.float32), device="cuda") for s in shapes]
+    xs = [W.clone().requires_grad_(True) for W in Ws]
+    outs = quant.bcjr_quantize_layer(xs, sls, srs, cb, T)
+    sum((o * g).sum() for o, g in zip(outs, Gs)).backward()
+    for W, sl, sr, G, o, x in zip(Ws, sls, srs, Gs, outs, xs):
+        y = W.clone().requires_grad_(True)
+        ref = quant.bcjr_quantize_weight(y, sl, sr, cb, T)
+        (ref * G).sum().backward()
+        assert torch.equal(o.detach(), ref.detach())
+        assert torch.equal(x.grad, y.grad)
