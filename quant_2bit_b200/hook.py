@@ -15,6 +15,10 @@ What is replaced (module attributes, looked up by the reference at call time):
   src.qat.quantized_linear imported from it (src/bcjr/bcjr_quant.py:159-178,
   src/qat/quantized_linear.py:41): RHT, RMS scale and tiling on both sides
   of the op run as native kernels;
+* the hard quantizer of src.qat.ste (viterbi_encode_chunked,
+  quantize_forward_gpu[_no_rht], TrellisQuantSTE[_IP]; src/qat/ste.py:58-356)
+  and the names src.qat.quantized_linear and src.bcjr.anneal import from it:
+  Viterbi encode, RHT, scale and tiling as native kernels;
 * src.bcjr.bcjr_monolithic.BcjrForwardBackwardMonolithic and
   bcjr_forward_backward_monolithic (src/bcjr/bcjr_monolithic.py:157-262);
 * src.bcjr.bcjr_quant.apply_rht_gpu / apply_inverse_rht_gpu and the same
@@ -27,6 +31,7 @@ import importlib
 
 from . import bcjr as _bcjr
 from . import quant as _quant
+from . import ste as _ste
 
 _saved = {}
 
@@ -49,11 +54,19 @@ def install(patch_rht=None):
     _patch(bq, "_bcjr_chunk_forward", _quant._bcjr_chunk_forward)
     _patch(bq, "bcjr_quantize_tiles", _quant.bcjr_quantize_tiles)
     _patch(bq, "bcjr_quantize_weight", _quant.bcjr_quantize_weight)
-    try:
-        ql = importlib.import_module("src.qat.quantized_linear")
-        _patch(ql, "bcjr_quantize_weight", _quant.bcjr_quantize_weight)
-    except Exception:       # optional: its imports may need packages not present
-        pass
+    for name in ("viterbi_encode_chunked", "quantize_forward_gpu", "quantize_forward_gpu_no_rht",
+                 "TrellisQuantSTE", "TrellisQuantSTE_IP"):
+        _patch(ste, name, getattr(_ste, name))
+    for modname, names in (("src.qat.quantized_linear",
+                            ("bcjr_quantize_weight", "TrellisQuantSTE", "TrellisQuantSTE_IP")),
+                           ("src.bcjr.anneal", ("TrellisQuantSTE",))):
+        try:
+            mod = importlib.import_module(modname)
+        except Exception:   # optional: its imports may need packages not present
+            continue
+        for name in names:
+            if hasattr(mod, name):
+                _patch(mod, name, getattr(_ste, name, None) or getattr(_quant, name))
     if bm is not None:
         _patch(bm, "BcjrForwardBackwardMonolithic", _bcjr.BcjrForwardBackwardMonolithic)
         _patch(bm, "bcjr_forward_backward_monolithic", _bcjr.bcjr_forward_backward_monolithic)

@@ -55,6 +55,9 @@ def test_hook_patches_reference_modules():
         assert "src.bcjr.bcjr_quant.bcjr_quantize_weight" in names
         assert bq._bcjr_chunk_forward is quant._bcjr_chunk_forward
         assert bq.bcjr_quantize_weight is quant.bcjr_quantize_weight
+        from quant_2bit_b200 import ste as qste
+        assert ste.TrellisQuantSTE is qste.TrellisQuantSTE
+        assert ste.viterbi_encode_chunked is qste.viterbi_encode_chunked
         assert bq.bcjr_quantize_tiles is quant.bcjr_quantize_tiles
         if not getattr(ste, "_HAS_FHT", False):
             assert bq.apply_rht_gpu is quant.apply_rht_gpu
