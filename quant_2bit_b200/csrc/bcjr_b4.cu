@@ -219,10 +219,10 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             const int r = (int)rank * kRPC + arl[h] + 16 * rr;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float2 u = __ldg(cb2 + (2 * i) * kG + 16 * r + ac[h]);
-                const float2 v = __ldg(cb2 + (2 * i + 1) * kG + 16 * r + ac[h]);
-                C0[h][rr][i] = mk(u.x, v.x);
-                C1[h][rr][i] = mk(u.y, v.y);
+                const float *u = reinterpret_cast<const float *>(cb2 + (2 * i) * kG + 16 * r + ac[h]);
+                const float *v = reinterpret_cast<const float *>(cb2 + (2 * i + 1) * kG + 16 * r + ac[h]);
+                C0[h][rr][i] = ldg_pair(u, v);
+                C1[h][rr][i] = ldg_pair(u + 1, v + 1);
             }
         }
     };
@@ -232,12 +232,11 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
             const int r = (int)rank * kRPC + brl + rr;
-            const float4 *base = reinterpret_cast<const float4 *>(cb2 + bp[h] * kG + 16 * r);
+            const float *base = reinterpret_cast<const float *>(cb2 + bp[h] * kG + 16 * r);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float4 v = __ldg(base + i);
-                C0[h][rr][i] = mk(v.x, v.z);
-                C1[h][rr][i] = mk(v.y, v.w);
+                C0[h][rr][i] = ldg_pair(base + 4 * i, base + 4 * i + 2);
+                C1[h][rr][i] = ldg_pair(base + 4 * i + 1, base + 4 * i + 3);
             }
         }
     };

@@ -130,6 +130,22 @@ __device__ __forceinline__ void wait_bar(uint32_t bar, uint32_t parity, int *sta
 // f32x2 pairs (FADD2 / FMUL2 / FFMA2 through the sm_100 float2 builtins).
 using F2 = float2;
 __device__ __forceinline__ F2 mk(float a, float b) { return make_float2(a, b); }
+
+// One float through the read-only path, as a load of its own (opaque to the
+// load vectoriser).  A register-resident pair built from two such loads can
+// be allocated straight into the register pair that the f32x2 instructions
+// read.  Built from two lanes of different vector loads instead, the pair's
+// halves are pinned to non-adjacent registers, and under register pressure
+// the pair is re-formed with moves at every use (measured on B200: about two
+// extra instructions per f32x2 use of a codebook pair).
+__device__ __forceinline__ float ldg1(const float *p) {
+    float v;
+    asm("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ F2 ldg_pair(const float *p0, const float *p1) {
+    return make_float2(ldg1(p0), ldg1(p1));
+}
 __device__ __forceinline__ F2 bc(float a) { return make_float2(a, a); }
 __device__ __forceinline__ F2 add2(F2 a, F2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ F2 sub2(F2 a, F2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }

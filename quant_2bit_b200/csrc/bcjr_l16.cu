@@ -179,16 +179,11 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
     for (int jj = 0; jj < kJPT; ++jj) {
         jg[jj] = (int)rank * kJPC + tid + kNT * jj;
-        float v[4][4];
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            const float4 q = __ldg(reinterpret_cast<const float4 *>(cb + p * kG + 4 * jg[jj]));
-            v[p][0] = q.x; v[p][1] = q.y; v[p][2] = q.z; v[p][3] = q.w;
-        }
+        const float *q = cb + 4 * jg[jj];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            cq[jj][c][0] = mk(v[0][c], v[1][c]);
-            cq[jj][c][1] = mk(v[2][c], v[3][c]);
+            cq[jj][c][0] = ldg_pair(q + c, q + kG + c);
+            cq[jj][c][1] = ldg_pair(q + 2 * kG + c, q + 3 * kG + c);
         }
     }
 

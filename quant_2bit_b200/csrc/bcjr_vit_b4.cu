@@ -96,10 +96,10 @@ vit_b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
         hg[rr] = 16 * r + ac;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const float2 u = __ldg(cb2 + (2 * i) * kG + 16 * r + ac);
-            const float2 v = __ldg(cb2 + (2 * i + 1) * kG + 16 * r + ac);
-            C0[rr][i] = mk(u.x, v.x);
-            C1[rr][i] = mk(u.y, v.y);
+            const float *u = reinterpret_cast<const float *>(cb2 + (2 * i) * kG + 16 * r + ac);
+            const float *v = reinterpret_cast<const float *>(cb2 + (2 * i + 1) * kG + 16 * r + ac);
+            C0[rr][i] = ldg_pair(u, v);
+            C1[rr][i] = ldg_pair(u + 1, v + 1);
         }
     }
 
