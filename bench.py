@@ -61,13 +61,14 @@ VITERBI_METRIC = "Viterbi (min-sum) state-transitions/sec (L=16,k=2,V=2), 1 B200
 MUFU = {1: (3.5, 4.0), 2: (3.125, 3.25)}
 MUFU_PER_SM_CLK = 16
 # dram__bytes_read.sum + dram__bytes_write.sum per sequence of the cluster
-# kernels, from one ncu capture of a 296-sequence launch of each
-# (profiles/); traffic grows in proportion to sequences.  V=1: L=16, N=256
-# (2-CTA clusters); V=2: L=16, N=128 (the history rows mostly stay in L2).
+# kernels, from one ncu capture of a small launch of each (profiles/);
+# traffic grows in proportion to sequences.  V=1: L=16, N=256, 296 sequences
+# (2-CTA clusters); V=2: L=16, N=128, 297 sequences (part of the history rows
+# stays in L2).
 DRAM_BYTES_PER_SEQ = {1: {"forward": (4.822843e9 + 4.961722e9) / 296,
                           "backward": (9.663011e9 + 9.910032e9) / 296},
-                      2: {"forward": (0.219314e9 + 0.564500e9) / 296,
-                          "backward": (0.830065e9 + 1.220563e9) / 296}}
+                      2: {"forward": (0.364880e9 + 0.627745e9) / 297,
+                          "backward": (0.998954e9 + 1.249169e9) / 297}}
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -668,8 +669,8 @@ def main():
             "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "Gop/s", "frac": achieved / peak,
                          "traffic": DRAM_BYTES_PER_SEQ[V][dom] * Bl if DRAM_BYTES_PER_SEQ[V] else None,
-                         "traffic_unit": "bytes per launch (ncu, 296-sequence capture scaled by "
-                                         "sequences; see profiles/)",
+                         "traffic_unit": "bytes per launch (ncu capture of 296 / 297 sequences "
+                                         "scaled by sequences; see profiles/)",
                          "note": f"algorithmic MUFU ops: {MUFU_FWD}/{MUFU_BWD} per state-step "
                                  f"(fwd/bwd call), peak = {sms} SMs x 16/clk x {clk_mhz:.0f} MHz"},
             "e2e": {"value": e2e_value, "unit": UNIT,
