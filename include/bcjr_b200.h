@@ -212,6 +212,14 @@ BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L
                           int *bitstreams, int *start_states, float *recons, float *mses,
                           void *ws, size_t ws_bytes, bcjr_stream_t stream);
 
+/* HYB codebook: cb_out (2^L x 2 fp32, device) from lut (2^Q x 2 fp32,
+ * device): for each state s, x = (s*s + s) mod 2^32, row = (x >> (15 - Q))
+ * mod 2^Q, cb_out[s] = (lut[row][0], +-lut[row][1]) with the sign flipped
+ * when bit 15 of x is set.  1 <= Q <= 15, 1 <= L <= 24; both pointers 8-byte
+ * aligned.  Replaces make_hyb_codebook_gpu (src/qat/ste.py:376-392) and
+ * decode_hyb_batch (src/codes/ref.py:116-128); bit-identical to both. */
+BCJR_API int bcjr_hyb_codebook(const float *lut, int Q, int L, float *cb_out, bcjr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,6 +43,7 @@ SIGNATURES = {
     "bcjr_untile_irht": ([_P, _P, _P, _I, _I, _P, _P, _P, _SZ, _P], _I),
     "bcjr_viterbi_workspace_bytes": ([_I, _I, _I, _I, _I], _SZ),
     "bcjr_viterbi": ([_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _SZ, _P], _I),
+    "bcjr_hyb_codebook": ([_P, _I, _I, _P, _P], _I),
 }
 
 _lib = None

@@ -18,7 +18,9 @@ What is replaced (module attributes, looked up by the reference at call time):
 * the hard quantizer of src.qat.ste (viterbi_encode_chunked,
   quantize_forward_gpu[_no_rht], TrellisQuantSTE[_IP]; src/qat/ste.py:58-356)
   and the names src.qat.quantized_linear and src.bcjr.anneal import from it:
-  Viterbi encode, RHT, scale and tiling as native kernels;
+  Viterbi encode, RHT, scale and tiling as native kernels; and
+  make_hyb_codebook_gpu (src/qat/ste.py:376-392), the HYB codebook built
+  from its LUT by one kernel;
 * src.bcjr.bcjr_monolithic.BcjrForwardBackwardMonolithic and
   bcjr_forward_backward_monolithic (src/bcjr/bcjr_monolithic.py:157-262);
 * src.bcjr.bcjr_quant.apply_rht_gpu / apply_inverse_rht_gpu and the same
@@ -55,7 +57,7 @@ def install(patch_rht=None):
     _patch(bq, "bcjr_quantize_tiles", _quant.bcjr_quantize_tiles)
     _patch(bq, "bcjr_quantize_weight", _quant.bcjr_quantize_weight)
     for name in ("viterbi_encode_chunked", "quantize_forward_gpu", "quantize_forward_gpu_no_rht",
-                 "TrellisQuantSTE", "TrellisQuantSTE_IP"):
+                 "TrellisQuantSTE", "TrellisQuantSTE_IP", "make_hyb_codebook_gpu"):
         _patch(ste, name, getattr(_ste, name))
     for modname, names in (("src.qat.quantized_linear",
                             ("bcjr_quantize_weight", "TrellisQuantSTE", "TrellisQuantSTE_IP")),

@@ -9,7 +9,7 @@ Same names, arguments and results as the reference:
 * quantize_forward_gpu_no_rht / quantize_forward_gpu (:160-210);
 * TrellisQuantSTE / TrellisQuantSTE_IP (:286-356): hard quantization forward,
   straight-through backward;
-* make_hyb_codebook_gpu (:376-392).
+* make_hyb_codebook_gpu (:376-392), on the native expansion kernel.
 The reference needs the fast_hadamard_transform extension on this path and
 falls back to numpy on the CPU; here everything runs on the GPU and CPU
 tensors raise.
@@ -17,6 +17,7 @@ tensors raise.
 import numpy as np
 import torch
 
+from . import _lib
 from . import quant as _q
 from .viterbi import viterbi_encode_v_batched_cuda
 
@@ -95,15 +96,20 @@ class TrellisQuantSTE_IP(torch.autograd.Function):
 
 
 def make_hyb_codebook_gpu(lut_np, Q=9, L_bits=L_BITS, device="cuda"):
-    """(2^L, 2) HYB codebook from a (2^Q, 2) LUT (src/qat/ste.py:376-392):
-    hash x = s*s + s mod 2^32, row (x >> (15 - Q)) & (2^Q - 1), second
-    component negated when bit 15 of x is set."""
-    lut = torch.as_tensor(np.asarray(lut_np, dtype=np.float32), device=device).contiguous()
-    s = torch.arange(1 << L_bits, dtype=torch.int64, device=device)
-    x = (s * s + s) & 0xFFFFFFFF
-    idx = (x >> (15 - Q)) & ((1 << Q) - 1)
-    sign = torch.where(((x >> 15) & 1).bool(), -1.0, 1.0).to(lut.dtype)
-    return torch.stack([lut[idx, 0], lut[idx, 1] * sign], dim=-1).contiguous()
+    """(2^L, 2) HYB codebook from a (2^Q, 2) LUT (src/qat/ste.py:376-392) by
+    the native expansion kernel (bcjr_hyb_codebook): hash x = s*s + s mod
+    2^32, row (x >> (15 - Q)) & (2^Q - 1), second component negated when bit
+    15 of x is set."""
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        raise RuntimeError("make_hyb_codebook_gpu builds the codebook on a CUDA device (there is no CPU path)")
+    lut = torch.as_tensor(np.asarray(lut_np, dtype=np.float32)).to(dev).contiguous()
+    assert lut.shape == (1 << Q, 2), f"LUT shape mismatch: {tuple(lut.shape)}"
+    cb = torch.empty((1 << L_bits, 2), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().bcjr_hyb_codebook(_lib.ptr(lut), Q, L_bits, _lib.ptr(cb),
+                                                 _lib.stream_ptr(dev)), "bcjr_hyb_codebook")
+    return cb
 
 
 __all__ = ["VITERBI_CHUNK", "viterbi_encode_chunked", "quantize_forward_gpu_no_rht",

@@ -58,6 +58,7 @@ def test_hook_patches_reference_modules():
         from quant_2bit_b200 import ste as qste
         assert ste.TrellisQuantSTE is qste.TrellisQuantSTE
         assert ste.viterbi_encode_chunked is qste.viterbi_encode_chunked
+        assert ste.make_hyb_codebook_gpu is qste.make_hyb_codebook_gpu
         assert bq.bcjr_quantize_tiles is quant.bcjr_quantize_tiles
         if not getattr(ste, "_HAS_FHT", False):
             assert bq.apply_rht_gpu is quant.apply_rht_gpu

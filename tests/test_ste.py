@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import hyb_codebook
+from conftest import hyb_codebook, load_golden
 from oracle import viterbi as ov
 
 pytestmark = pytest.mark.gpu
@@ -68,3 +68,30 @@ def test_make_hyb_codebook_gpu(cuda_ok):
     from quant_2bit_b200 import ste
     lut, cb, _, _, _ = _setup(16, 16, 1)
     assert torch.equal(ste.make_hyb_codebook_gpu(lut), cb)
+
+
+def test_hyb_codebook_matches_reference_decoder(cuda_ok):
+    """The expansion kernel against rows of the codebook the reference's
+    decode_hyb_batch (src/codes/ref.py:116-128) built from the same LUT."""
+    from quant_2bit_b200 import ste
+    d = load_golden("l16v2_hyb_T0.3.npz")
+    cb = ste.make_hyb_codebook_gpu(d["lut"]).cpu().numpy()
+    np.testing.assert_array_equal(cb[d["cb_rows"]], d["cb_at_rows"])
+
+
+@pytest.mark.parametrize("Q,L", [(1, 4), (9, 8), (9, 16), (12, 16), (15, 16), (9, 20)])
+def test_hyb_codebook_shapes(cuda_ok, Q, L):
+    from quant_2bit_b200 import ste
+    lut = np.random.default_rng(Q * 100 + L).standard_normal((1 << Q, 2)).astype(np.float32)
+    got = ste.make_hyb_codebook_gpu(lut, Q=Q, L_bits=L).cpu().numpy()
+    np.testing.assert_array_equal(got, hyb_codebook(lut, Q=Q, L=L))
+
+
+def test_hyb_codebook_errors(cuda_ok):
+    from quant_2bit_b200 import ste
+    with pytest.raises(AssertionError):
+        ste.make_hyb_codebook_gpu(np.zeros((64, 2), np.float32), Q=9)
+    with pytest.raises(AssertionError):
+        ste.make_hyb_codebook_gpu(np.zeros((1 << 16, 2), np.float32), Q=16)
+    with pytest.raises(RuntimeError):
+        ste.make_hyb_codebook_gpu(np.zeros((512, 2), np.float32), device="cpu")
