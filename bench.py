@@ -588,6 +588,10 @@ def main():
         dist.barrier()
     clk = clocks.stop()
 
+    # kernels of one forward + backward call pair (the backward of L=16, V=1
+    # runs two grids side by side above one round of the 2-CTA grid)
+    launches_per_step = (lib.bcjr_kernel_launches(Bl, NSTEP, L, K_BITS, V, _lib.WS_FORWARD) +
+                         lib.bcjr_kernel_launches(Bl, NSTEP, L, K_BITS, V, _lib.WS_BACKWARD))
     step_ms = [e[0].elapsed_time(e[3]) for e in events]
     fwd_ms = [e[0].elapsed_time(e[1]) for e in events]
     bwd_ms = [e[1].elapsed_time(e[2]) for e in events]
@@ -664,7 +668,7 @@ def main():
                        "l2": "flushed between timed steps (256 MB write, outside the events)",
                        "collective": "NCCL all_gather of soft per step" if world > 1 else "none"},
             "clocks": clk,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "kernel_ms": {"forward": fwd_avg, "backward": bwd_avg},
             "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "Gop/s", "frac": achieved / peak,

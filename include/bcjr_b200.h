@@ -76,6 +76,12 @@ BCJR_API size_t bcjr_workspace_bytes(int B, int N, int L, int k, int V, int flag
 /* Shape validation without launching anything: BCJR_OK or the error code. */
 BCJR_API int bcjr_check_shape(int B, int N, int L, int k, int V);
 
+/* Kernel launches one call of the entry point named by `flags`
+ * (BCJR_WS_FORWARD, BCJR_WS_BACKWARD or BCJR_WS_INTERNALS, one of them)
+ * makes for this problem on the current device, with a 16-byte aligned
+ * codebook; 0 for an invalid shape.  For profiling and launch accounting. */
+BCJR_API int bcjr_kernel_launches(int B, int N, int L, int k, int V, int flags);
+
 /*
  * Forward: soft[b,t,:] = sum_s P_t(s) c(s)  and  logZ[b] (natural log).
  *   seq   (B, N, V)   input sequences (the 16x16 weight tiles)

@@ -32,6 +32,7 @@ SIGNATURES = {
     "bcjr_status_string": ([_I], ctypes.c_char_p),
     "bcjr_workspace_bytes": ([_I, _I, _I, _I, _I, _I], _SZ),
     "bcjr_check_shape": ([_I, _I, _I, _I, _I], _I),
+    "bcjr_kernel_launches": ([_I, _I, _I, _I, _I, _I], _I),
     "bcjr_fb_forward": ([_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _SZ, _P], _I),
     "bcjr_fb_backward": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P], _I),
     "bcjr_fb_internals": ([_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P], _I),

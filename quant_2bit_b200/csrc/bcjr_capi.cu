@@ -13,7 +13,7 @@
 
 namespace {
 
-constexpr size_t kHeaderBytes = 256;  // status word + padding (keeps data 256-B aligned)
+constexpr size_t kHeaderBytes = 256;  // status word, sequence counter, padding (keeps data 256-B aligned)
 
 struct DevInfo {
     int sms = 0;
@@ -109,6 +109,7 @@ int prepare(bcjr::LaunchArgs &a, void *ws, size_t ws_bytes, int mode) {
                             : kernel_bytes(a.kernel, a.B, a.N, a.L, a.BB, a.V, mode, d.sms);
     if (ws_bytes < kHeaderBytes + need) return BCJR_ERR_WORKSPACE;
     a.status = reinterpret_cast<int *>(ws);
+    a.claim = reinterpret_cast<unsigned *>(static_cast<char *>(ws) + sizeof(int));
     a.ws_data = static_cast<char *>(ws) + kHeaderBytes;
     a.ws_data_bytes = ws_bytes - kHeaderBytes;
     a.mode = mode;
@@ -118,7 +119,8 @@ int prepare(bcjr::LaunchArgs &a, void *ws, size_t ws_bytes, int mode) {
     a.drop_sends = (drop && drop[0] == '1') ? 1 : 0;
     a.grid = a.kernel != bcjr::kKernelGeneric ? 1 : bcjr::generic_grid(a.B, a.N, a.L, a.BB, mode, a.ws_data_bytes);
     if (a.grid < 1) return BCJR_ERR_WORKSPACE;
-    if (cudaMemsetAsync(a.status, 0, sizeof(int), a.stream) != cudaSuccess) return BCJR_ERR_LAUNCH;
+    if (cudaMemsetAsync(a.status, 0, sizeof(int) + sizeof(unsigned), a.stream) != cudaSuccess)
+        return BCJR_ERR_LAUNCH;
     return BCJR_OK;
 }
 
@@ -156,6 +158,20 @@ const char *bcjr_status_string(int status) {
 }
 
 int bcjr_check_shape(int B, int N, int L, int k, int V) { return check_shape(B, N, L, k, V); }
+
+int bcjr_kernel_launches(int B, int N, int L, int k, int V, int flags) {
+    if (check_shape(B, N, L, k, V) || B == 0) return 0;
+    DevInfo d;
+    if (query_device(d)) return 0;
+    const int mode = flags == BCJR_WS_FORWARD    ? bcjr::kModeForward
+                     : flags == BCJR_WS_BACKWARD ? bcjr::kModeBackward
+                     : flags == BCJR_WS_INTERNALS ? bcjr::kModeInternals
+                                                  : -1;
+    if (mode < 0) return 0;
+    const int b = k * V;
+    if (pick_kernel(B, N, L, b, V, mode, nullptr) == bcjr::kKernelL16) return bcjr::l16_launches(B, mode);
+    return 1;
+}
 
 size_t bcjr_workspace_bytes(int B, int N, int L, int k, int V, int flags) {
     if (check_shape(B, N, L, k, V)) return 0;

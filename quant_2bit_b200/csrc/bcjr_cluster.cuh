@@ -74,6 +74,9 @@ __device__ __forceinline__ void st_async1(uint32_t addr, float a, uint32_t bar) 
 __device__ __forceinline__ void st_cluster(uint32_t addr, float a) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(a) : "memory");
 }
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t a) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(a) : "memory");
+}
 // One TMA bulk copy global -> own shared memory, completing on `bar`.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
                                          uint32_t bar) {

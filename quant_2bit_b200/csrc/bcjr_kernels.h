@@ -19,6 +19,7 @@ struct LaunchArgs {
     void *ws_data;                // workspace after the header
     size_t ws_data_bytes;
     int *status;                  // device status word in the workspace header
+    unsigned *claim;              // device sequence counter in the header (zeroed per call)
     int mode;
     int grid;
     int kernel;                   // kKernelGeneric / kKernelL16 / kKernelB4
@@ -31,9 +32,24 @@ size_t generic_workspace_bytes(int B, int N, int L, int BB, int V, int mode, int
 int generic_grid(int B, int N, int L, int BB, int mode, size_t ws_data_bytes);
 cudaError_t launch_generic(const LaunchArgs &a);
 
-// Cluster path for L=16, k=2, V=1, 2 <= N <= 512 (bcjr_l16.cu).
+// Cluster path for L=16, k=2, V=1, 2 <= N <= 512 (bcjr_l16.cu): the 2-CTA
+// (l16) and 4-CTA (l16c4, bcjr_l16_cl4.cu) instances of one kernel, and the
+// dispatcher that runs one or both.
+namespace l16 {
+int max_clusters(int mode);
+int slots(int mode);
+size_t slot_bytes(int N, int mode);
+cudaError_t launch(const LaunchArgs &a, int ncl, float *ws, bool dependent);
+}  // namespace l16
+namespace l16c4 {
+int max_clusters(int mode);
+int slots(int mode);
+size_t slot_bytes(int N, int mode);
+cudaError_t launch(const LaunchArgs &a, int ncl, float *ws, bool dependent);
+}  // namespace l16c4
 bool l16_applicable(int B, int N, int L, int BB, int V);
 int l16_clusters(int B, int mode);
+int l16_launches(int B, int mode);
 size_t l16_workspace_bytes(int B, int N, int mode);
 cudaError_t launch_l16(const LaunchArgs &a);
 

@@ -1,8 +1,9 @@
-// Production kernel for the QTIP trellis L=16, k=2, V=1 (b = 2): one
-// 2-CTA thread-block cluster per pair of sequences (forward) or per sequence
-// (backward), one CTA per SM.  Clusters of 2 tile all 148 SMs of a B200
-// (74 clusters); clusters of 4 fit only 33 (132 SMs), and measured 14 %
-// slower (BCJR_L16_CL=4 still builds that variant).
+// Production kernel for the QTIP trellis L=16, k=2, V=1 (b = 2), one CTA per
+// SM, in two instances: 2-CTA thread-block clusters (all 148 SMs of a B200,
+// 74 clusters; two sequences in flight per cluster in the forward, one in the
+// backward) and 4-CTA clusters (33 clusters on 132 SMs; two sequences in both
+// calls).  The forward runs the 2-CTA instance; the backward runs the 4-CTA
+// grid and, on the 16 SMs it leaves free, a 2-CTA grid beside it.
 //
 // Work decomposition
 // ------------------
@@ -48,19 +49,34 @@
 // Alpha / H rows go to a global history with float4 stores; the
 // backward-time sweep fetches
 // the rows it needs one step ahead with TMA bulk copies (cp.async.bulk) into
-// shared memory.  Per-step partial sums of soft / d_seq are written per CTA
-// and added in a fixed order by CTA 0: results are deterministic.
+// shared memory.  Per-step partial sums of soft / d_seq are written per
+// (block of 1024 butterflies, warp) and added in a fixed order by CTA 0, log Z
+// likewise: results are deterministic and the same in both instances, so
+// sequences may go to either (they are claimed from a shared counter).
 //
 // Every wait is bounded (about 1 s); on timeout the kernel records
 // BCJR_ERR_TIMEOUT in the workspace status word, stops waiting and sending,
 // and runs to completion.  The recursions are documented in bcjr_common.cuh.
 #include <cstdint>
+#include <cstdlib>
 
 #include "bcjr_cluster.cuh"
 #include "bcjr_kernels.h"
 
+// This file is compiled twice: as the 2-CTA instance (namespace l16, which
+// also holds the dispatcher at the end) and, from bcjr_l16_cl4.cu, as the
+// 4-CTA instance (namespace l16c4).
+#ifndef BCJR_L16_CL
+#define BCJR_L16_CL 2
+#endif
+#if BCJR_L16_CL == 2
+#define BCJR_L16_NS l16
+#else
+#define BCJR_L16_NS l16c4
+#endif
+
 namespace bcjr {
-namespace l16 {
+namespace BCJR_L16_NS {
 
 using namespace clu;
 
@@ -68,9 +84,6 @@ constexpr int kL = 16;
 constexpr int kB = 2;                 // branch bits b = kV
 constexpr int kG = 1 << (kL - kB);    // 16384 groups
 constexpr int kNJ = kG >> kB;         // 4096 butterflies
-#ifndef BCJR_L16_CL
-#define BCJR_L16_CL 2
-#endif
 constexpr int kCL = BCJR_L16_CL;      // CTAs per cluster (4 or 2)
 constexpr int kJPC = kNJ / kCL;       // butterflies per CTA
 constexpr int kIn = 4 * kJPC;         // inputs per CTA per step and plane
@@ -96,6 +109,15 @@ struct SleepOf {
     static constexpr unsigned value = SlotsOf<GRAD>::value == 1 ? BCJR_L16_SLEEP1_NS : kWaitSleepNs;
 };
 constexpr int kWarps = kNT / 32;
+// Reduction blocks: the per-step sums (soft codewords, gradients) and log Z
+// are reduced per block of 1024 butterflies and warp, then over the 4 x 16
+// (block, warp) partials in a fixed order.  A thread's butterflies
+// tid + 512 jj fall in block (rank kJPC + 512 jj) / 1024, two per block, in
+// both instances, so a sequence's results are bitwise the same whichever
+// instance runs it.
+constexpr int kRB = kNJ / 1024;       // 4 reduction blocks
+constexpr int kParts = kRB * kWarps;  // 64 partials per step
+static_assert(kJPT % 2 == 0, "two butterflies of a thread per reduction block");
 
 template <bool GRAD>
 struct alignas(128) Smem {
@@ -108,13 +130,12 @@ struct alignas(128) Smem {
     float w[kSlots][kNMax];
     float g[kSlots][GRAD ? kNMax : 4];
     float sf[kSlots][GRAD ? kNMax : 4];
-    float wmin[kSlots][kWarps];
-    float wacc[kSlots][kWarps];
-    float lz[kSlots][kCL][2];
+    float lz[kSlots][kParts][2];          // log Z partials, every (block, warp) of the cluster
     unsigned long long full[kSlots][2];
     unsigned long long hbar[kSlots];
     int cnt[kSlots][2];                   // warps finished with the step (backward sweep)
     int hiss[kSlots];                     // TMA row loads issued per slot
+    unsigned next;                        // first sequence of the cluster's current claim
 };
 
 // Minimum of the kCL * kWarps per-warp minima riding with a consumption
@@ -130,7 +151,7 @@ __device__ __forceinline__ float cluster_min(const float *m, int lane) {
 struct SlotLayout {
     long hist;      // alpha cost rows: N x kG  (row t holds S_t, t >= 1)
     long hhist;     // H rows: N x kG  (backward only)
-    long part;      // N x kCL x kWarps per-step per-warp partial sums
+    long part;      // N x kParts per-step (block, warp) partial sums
     long total;
 };
 
@@ -139,7 +160,7 @@ __host__ __device__ inline SlotLayout slot_layout(int N, bool grad) {
     long p = 0;
     s.hist = p; p += (long)N * kG;
     s.hhist = p; if (grad) p += (long)N * kG;
-    s.part = p; p += (long)N * kCL * kWarps;
+    s.part = p; p += (long)N * kParts;
     s.total = (p + 63) & ~63L;   // 256-byte aligned slots
     return s;
 }
@@ -150,9 +171,14 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
            const float *__restrict__ T_dev, const float *__restrict__ soft_in,
            const float *__restrict__ grad, int B, int N,
            float *__restrict__ out, float *__restrict__ logZ_out,
-           float *__restrict__ ws, int *status, int drop_sends) {
+           float *__restrict__ ws, int *status, unsigned *claim, int drop_sends) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     using SM = Smem<GRAD>;
+    // A kernel launched after this one with programmatic stream serialization
+    // (the 2-CTA backward on the SMs that 4-CTA clusters leave free) may start
+    // now; it takes sequences from the same counter and waits for this grid
+    // before it completes.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     SM &sm = *reinterpret_cast<SM *>(smem_raw);
     constexpr int kPlanes = SM::kPlanes;
     constexpr int kSlots = SM::kSlots;
@@ -163,7 +189,6 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     const int lane = tid & 31, warp = tid >> 5;
     const uint32_t rank = cluster_rank();
     const uint32_t cid = cluster_id();
-    const uint32_t ncl = num_clusters();
     const SlotLayout lay = slot_layout(N, GRAD);
 
     const float T = __ldg(T_dev);
@@ -255,8 +280,8 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         }
     };
 
-    auto finish_step = [&](int z, int nb, bool send, float lmin, float *part_row, float acc,
-                           int rows_tn, float *const *slot_ws) {
+    auto finish_step = [&](int z, int nb, bool send, float lmin, int rows_tn,
+                           float *const *slot_ws) {
         // The warp's minimum output cost goes to every consumer CTA with the
         // data (part of the consumption's byte count).  Sent after the warp
         // has read this step's inputs, it also tells every producer that the
@@ -266,11 +291,6 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             const uint32_t peer = mapa(sbase, (uint32_t)lane);
             st_async1(peer + soff(&sm.maxslot[z][nb][rank * kWarps + warp]), wmin,
                       peer + soff(&sm.full[z][nb]));
-        }
-        if (part_row) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            if (lane == 0) part_row[warp] = acc;
         }
         if (rows_tn >= 1) {
             // the last warp to finish the step has the staged history row to
@@ -289,13 +309,25 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         }
     };
 
-    for (long pair = cid; pair * kSlots < B; pair += ncl) {
+    // Sequences are claimed kSlots at a time from a counter shared by every
+    // cluster of the call (of both instances, when two run side by side):
+    // CTA 0 takes the claim and publishes it to the cluster.
+    auto claim_next = [&]() -> long {
+        if (rank == 0 && tid == 0) {
+            const unsigned s0 = failed ? 0x7fffffffu : atomicAdd(claim, (unsigned)kSlots);
+#pragma unroll
+            for (int r = 0; r < kCL; ++r) st_cluster_u32(cbase[r] + soff(&sm.next), s0);
+        }
+        cluster_sync();
+        return (long)sm.next;
+    };
+    for (long first = claim_next(); first < B; first = claim_next()) {
         bool active[kSlots];
         long sidx[kSlots];
         float *slot_ws[kSlots];
 #pragma unroll
         for (int z = 0; z < kSlots; ++z) {
-            sidx[z] = pair * kSlots + z;
+            sidx[z] = first + z;
             active[z] = sidx[z] < B;
             slot_ws[z] = ws + ((long)cid * kSlots + z) * lay.total;
         }
@@ -315,9 +347,8 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 
         // ------------------------------------------------------------ alpha
         double O[kSlots];
-        float lzm[kSlots], lzs[kSlots];
 #pragma unroll
-        for (int z = 0; z < kSlots; ++z) { O[z] = 0.0; lzm[z] = kPosInf; lzs[z] = 0.f; }
+        for (int z = 0; z < kSlots; ++z) O[z] = 0.0;
         for (int t = 0; t < N; ++t) {
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
@@ -350,6 +381,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 const uint32_t buf_off = soff(&sm.buf[z][nb][0][0]);
                 const F2 W = bc(w), Gq = bc(gq), GS = bc(-gs), NK = bc(-kap);
                 float lmin = kPosInf;
+                float lzm = kPosInf, lzs = 0.f;   // log Z soft-min of a block (last step)
                 float *hist = slot_ws[z] + lay.hist + (long)(t + 1) * kG;
                 float *hhist = slot_ws[z] + lay.hhist + (long)(t + 1) * kG;
 #pragma unroll
@@ -398,42 +430,34 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                         if (GRAD)
                             *reinterpret_cast<float4 *>(hhist + 4 * j) = make_float4(h4[0], h4[1], h4[2], h4[3]);
                     } else {
+                        // log Z: soft-min of the last costs per (block, warp)
+                        if ((jj & 1) == 0) { lzm = kPosInf; lzs = 0.f; }
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) smin_merge(lzm[z], lzs[z], kap * o4[c], 1.f);
+                        for (int c = 0; c < 4; ++c) smin_merge(lzm, lzs, kap * o4[c], 1.f);
+                        if (jj & 1) {
+                            float m = lzm, s = lzs;
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) {
+                                const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+                                const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+                                smin_merge(m, s, m2, s2);
+                            }
+                            if (lane == 0) {
+                                const int part = ((int)rank * (kJPC / 1024) + (jj >> 1)) * kWarps + warp;
+#pragma unroll
+                                for (int r = 0; r < kCL; ++r) {
+                                    st_cluster(cbase[r] + soff(&sm.lz[z][part][0]), m);
+                                    st_cluster(cbase[r] + soff(&sm.lz[z][part][1]), s);
+                                }
+                            }
+                        }
                     }
                 }
-                finish_step(z, nb, !last && !drop, lmin, nullptr, 0.f, 0, slot_ws);
+                finish_step(z, nb, !last && !drop, lmin, 0, slot_ws);
             }
         }
-        __syncthreads();
-
-        // log2 Z = -(kappa O_{N-1} + log2-soft-min over all 16384 costs kappa S_N).
-#pragma unroll
-        for (int z = 0; z < kSlots; ++z) {
-            if (!active[z]) continue;
-            float m = lzm[z], s = lzs[z];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-                const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-                smin_merge(m, s, m2, s2);
-            }
-            if (lane == 0) { sm.wmin[z][warp] = m; sm.wacc[z][warp] = s; }
-        }
-        __syncthreads();
-        if (tid == 0) {
-#pragma unroll
-            for (int z = 0; z < kSlots; ++z) {
-                if (!active[z]) continue;
-                float m = kPosInf, s = 0.f;
-                for (int i = 0; i < kWarps; ++i) smin_merge(m, s, sm.wmin[z][i], sm.wacc[z][i]);
-#pragma unroll
-                for (int r = 0; r < kCL; ++r) {
-                    st_cluster(cbase[r] + soff(&sm.lz[z][rank][0]), m);
-                    st_cluster(cbase[r] + soff(&sm.lz[z][rank][1]), s);
-                }
-            }
-        }
+        // log2 Z = -(kappa O_{N-1} + log2-soft-min over all 16384 costs kappa S_N),
+        // the soft-min merged over the 64 (block, warp) partials in order.
         cluster_sync();   // also publishes every CTA's history rows
 
         double logZ2[kSlots];
@@ -443,8 +467,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         for (int z = 0; z < kSlots; ++z) {
             if (!active[z]) continue;
             float m = kPosInf, s = 0.f;
-#pragma unroll
-            for (int r = 0; r < kCL; ++r) smin_merge(m, s, sm.lz[z][r][0], sm.lz[z][r][1]);
+            for (int i = 0; i < kParts; ++i) smin_merge(m, s, sm.lz[z][i][0], sm.lz[z][i][1]);
             logZ2[z] = -((double)kap * O[z] + (double)m - (double)log2f(s));
             if (!GRAD && rank == 0 && tid == 0 && logZ_out)
                 logZ_out[sidx[z]] = (float)(logZ2[z] * (double)kLn2);
@@ -504,6 +527,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 for (int jj = 0; jj < kJPT; ++jj) {
                     const int j = jg[jj];
                     const int jl = tid + kNT * jj;
+                    if ((jj & 1) == 0) acc = bc(0.f);   // first butterfly of a reduction block
                     // my butterfly's inputs (minus the global minimum) and history values
                     float bin[4] = {0.f, 0.f, 0.f, 0.f}, bbin[4] = {0.f, 0.f, 0.f, 0.f};
                     if (in) {
@@ -585,14 +609,22 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                             }
                         }
                     }
+                    if (jj & 1) {
+                        // the (block, warp) partial of this step
+                        float v = acc.x + acc.y;
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                        if (lane == 0)
+                            slot_ws[z][lay.part + (long)tn * kParts +
+                                       ((int)rank * (kJPC / 1024) + (jj >> 1)) * kWarps + warp] = v;
+                    }
                 }
-                float *part_row = slot_ws[z] + lay.part + ((long)tn * kCL + rank) * kWarps;
-                finish_step(z, nb, t >= 0, lmin, part_row, acc.x + acc.y, tn - 1, slot_ws);
+                finish_step(z, nb, t >= 0, lmin, tn - 1, slot_ws);
             }
         }
         __syncthreads();
 
-        // Per-step partials of the 4 x 16 warps, added in a fixed order.
+        // Per-step partials of the 4 x 16 (block, warp) pairs, added in a fixed order.
         cluster_sync();
         if (rank == 0) {
             const float scale = GRAD ? two_over_T : 1.f;
@@ -601,10 +633,10 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 if (!active[z]) continue;
                 const float *part = slot_ws[z] + lay.part;
                 for (int tn = tid; tn < N; tn += kNT) {
-                    const float4 *p4 = reinterpret_cast<const float4 *>(part + (long)tn * kCL * kWarps);
+                    const float4 *p4 = reinterpret_cast<const float4 *>(part + (long)tn * kParts);
                     float sum = 0.f;
 #pragma unroll
-                    for (int i = 0; i < kCL * kWarps / 4; ++i) {
+                    for (int i = 0; i < kParts / 4; ++i) {
                         const float4 v = __ldcg(p4 + i);
                         sum += ((v.x + v.y) + v.z) + v.w;
                     }
@@ -624,46 +656,145 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 wait_bar<SleepOf<GRAD>::value>(sbase + soff(&sm.hbar[z]), k & 1, status, f2);
     }
     cluster_sync();
+    // Launched as the dependent of another grid (programmatic stream
+    // serialization), this grid completes only after that one has, so later
+    // work in the stream sees the results of both.  Otherwise a no-op.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
-}  // namespace l16
-
 // ---------------------------------------------------------------------------
-// Host side.
+// Host side of this instance.
 
 namespace {
 
 template <bool GRAD>
-int l16_max_clusters() {
+int max_clusters_of() {
     static int cached[2][64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     int &c = cached[GRAD ? 1 : 0][dev];
     if (c > 0) return c;
-    const size_t smem = sizeof(l16::Smem<GRAD>);
-    if (cudaFuncSetAttribute(l16::l16_kernel<GRAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const size_t smem = sizeof(Smem<GRAD>);
+    if (cudaFuncSetAttribute(l16_kernel<GRAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
         return 0;
     cudaLaunchConfig_t cfg = {};
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cfg.gridDim = dim3((unsigned)(sms / l16::kCL * l16::kCL), 1, 1);
-    cfg.blockDim = dim3(l16::kNT, 1, 1);
+    cfg.gridDim = dim3((unsigned)(sms / kCL * kCL), 1, 1);
+    cfg.blockDim = dim3(kNT, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = l16::kCL;
+    attr[0].val.clusterDim.x = kCL;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, l16::l16_kernel<GRAD>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, l16_kernel<GRAD>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
     c = n;
     return n;
+}
+
+template <bool GRAD>
+cudaError_t launch_of(const LaunchArgs &a, int ncl, float *ws, bool dependent) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(ncl * kCL), 1, 1);
+    cfg.blockDim = dim3(kNT, 1, 1);
+    cfg.dynamicSmemBytes = sizeof(Smem<GRAD>);
+    cfg.stream = a.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    if (GRAD)
+        return cudaLaunchKernelEx(&cfg, l16_kernel<GRAD>, a.seq, a.cb, a.T_dev, a.soft_in, a.grad,
+                                  a.B, a.N, a.dseq, (float *)nullptr, ws, a.status, a.claim,
+                                  a.drop_sends);
+    return cudaLaunchKernelEx(&cfg, l16_kernel<GRAD>, a.seq, a.cb, a.T_dev, (const float *)nullptr,
+                              (const float *)nullptr, a.B, a.N, a.soft, a.logZ, ws, a.status,
+                              a.claim, a.drop_sends);
+}
+
+}  // namespace
+
+int max_clusters(int mode) {
+    return mode == kModeBackward ? max_clusters_of<true>() : max_clusters_of<false>();
+}
+
+int slots(int mode) {
+    return mode == kModeBackward ? SlotsOf<true>::value : SlotsOf<false>::value;
+}
+
+size_t slot_bytes(int N, int mode) {
+    return (size_t)slot_layout(N, mode == kModeBackward).total * 4;
+}
+
+cudaError_t launch(const LaunchArgs &a, int ncl, float *ws, bool dependent) {
+    if (ncl <= 0) return cudaErrorInvalidConfiguration;
+    return a.mode == kModeBackward ? launch_of<true>(a, ncl, ws, dependent)
+                                   : launch_of<false>(a, ncl, ws, dependent);
+}
+
+}  // namespace BCJR_L16_NS
+
+#if BCJR_L16_CL == 2
+// ---------------------------------------------------------------------------
+// Dispatcher for L=16, k=2, V=1.
+//
+// Forward: the 2-CTA instance (two slots) on every SM.  Backward: the 2-CTA
+// instance has room for one slot, the 4-CTA instance for two but tiles only
+// 132 of the 148 SMs.  Both run side by side: the 4-CTA grid first, then the
+// 2-CTA grid on the SMs it leaves free, launched as its programmatic
+// dependent; both take sequences from one counter (measured on B200 with
+// 4096 sequences: 2-CTA alone 114 ms, 4-CTA alone 116 ms, both ~105 ms).
+// BCJR_B200_L16_BACKWARD=2 or =4 runs one instance alone in the backward,
+// BCJR_B200_L16_FORWARD=4 the 4-CTA instance in the forward (tests).  Results
+// do not depend on the instance that runs a sequence.
+
+namespace {
+
+struct Plan {
+    int n4 = 0;   // 4-CTA clusters
+    int n2 = 0;   // 2-CTA clusters
+};
+
+Plan plan_for(int B, int mode) {
+    Plan p;
+    const long b = B > 0 ? B : 1;
+    const bool bwd = mode == kModeBackward;
+    const char *env = std::getenv(bwd ? "BCJR_B200_L16_BACKWARD" : "BCJR_B200_L16_FORWARD");
+    const int force = env ? std::atoi(env) : 0;
+    const int max2 = l16::max_clusters(mode);
+    const long need2 = (b + l16::slots(mode) - 1) / l16::slots(mode);
+    const int max4 = l16c4::max_clusters(mode);
+    const long need4 = (b + l16c4::slots(mode) - 1) / l16c4::slots(mode);
+    if (force == 4 && max4 > 0) {
+        p.n4 = (int)(need4 < max4 ? need4 : max4);
+        return p;
+    }
+    // the forward, and a batch that one round of the 2-CTA instance covers:
+    // the 2-CTA instance alone
+    if (!bwd || force == 2 || max4 <= 0 || need2 <= max2) {
+        p.n2 = (int)(need2 < max2 ? need2 : max2);
+        return p;
+    }
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    p.n4 = max4;
+    p.n2 = (sms - 4 * max4) / 2;
+    if (p.n2 < 0) p.n2 = 0;
+    return p;
+}
+
+size_t region4(const Plan &p, int N, int mode) {
+    return ((size_t)p.n4 * l16c4::slots(mode) * l16c4::slot_bytes(N, mode) + 255) & ~(size_t)255;
 }
 
 }  // namespace
@@ -673,46 +804,36 @@ bool l16_applicable(int B, int N, int L, int BB, int V) {
     return L == l16::kL && BB == l16::kB && V == 1 && N >= 2 && N <= l16::kNMax;
 }
 
-namespace {
-int l16_slots(int mode) {
-    return mode == kModeBackward ? l16::SlotsOf<true>::value : l16::SlotsOf<false>::value;
-}
-}  // namespace
-
 int l16_clusters(int B, int mode) {
-    const int maxc = (mode == kModeBackward) ? l16_max_clusters<true>() : l16_max_clusters<false>();
-    const int slots = l16_slots(mode);
-    const long pairs = ((long)B + slots - 1) / slots;
-    long n = maxc;
-    if (n > pairs) n = pairs;
-    return (int)n;
+    const Plan p = plan_for(B, mode);
+    return p.n2 + p.n4;
 }
 
 size_t l16_workspace_bytes(int B, int N, int mode) {
-    const int ncl = l16_clusters(B, mode);
-    if (ncl <= 0) return 0;
-    const long slot = l16::slot_layout(N, mode == kModeBackward).total;
-    return (size_t)ncl * l16_slots(mode) * slot * 4;
+    const Plan p = plan_for(B, mode);
+    if (p.n2 + p.n4 <= 0) return 0;
+    return region4(p, N, mode) + (size_t)p.n2 * l16::slots(mode) * l16::slot_bytes(N, mode);
+}
+
+int l16_launches(int B, int mode) {
+    const Plan p = plan_for(B, mode);
+    return (p.n4 > 0) + (p.n2 > 0);
 }
 
 cudaError_t launch_l16(const LaunchArgs &a) {
-    const bool grad = (a.mode == kModeBackward);
-    const int ncl = l16_clusters(a.B, a.mode);
-    if (ncl <= 0) return cudaErrorInvalidConfiguration;
-    const long slot = l16::slot_layout(a.N, grad).total;
-    if ((size_t)ncl * l16_slots(a.mode) * slot * 4 > a.ws_data_bytes) return cudaErrorInvalidValue;
-    const dim3 grid((unsigned)(ncl * l16::kCL)), block(l16::kNT);
-    float *ws = reinterpret_cast<float *>(a.ws_data);
-    if (grad) {
-        l16::l16_kernel<true><<<grid, block, sizeof(l16::Smem<true>), a.stream>>>(
-            a.seq, a.cb, a.T_dev, a.soft_in, a.grad, a.B, a.N, a.dseq, nullptr, ws, a.status,
-            a.drop_sends);
-    } else {
-        l16::l16_kernel<false><<<grid, block, sizeof(l16::Smem<false>), a.stream>>>(
-            a.seq, a.cb, a.T_dev, nullptr, nullptr, a.B, a.N, a.soft, a.logZ, ws, a.status,
-            a.drop_sends);
+    const Plan p = plan_for(a.B, a.mode);
+    if (p.n2 + p.n4 <= 0) return cudaErrorInvalidConfiguration;
+    if (l16_workspace_bytes(a.B, a.N, a.mode) > a.ws_data_bytes) return cudaErrorInvalidValue;
+    char *ws = static_cast<char *>(a.ws_data);
+    cudaError_t e = cudaSuccess;
+    if (p.n4 > 0) {
+        e = l16c4::launch(a, p.n4, reinterpret_cast<float *>(ws), false);
+        if (e != cudaSuccess) return e;
     }
-    return cudaGetLastError();
+    if (p.n2 > 0)
+        e = l16::launch(a, p.n2, reinterpret_cast<float *>(ws + region4(p, a.N, a.mode)), p.n4 > 0);
+    return e;
 }
+#endif  // BCJR_L16_CL == 2
 
 }  // namespace bcjr

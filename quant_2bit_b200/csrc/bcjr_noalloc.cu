@@ -89,6 +89,7 @@ extern "C" BCJR_API int bcjr_fb_forward_noalloc(const float *seq, const float *c
     a.ws_data = scratch;
     a.ws_data_bytes = kNoAllocScratchBytes;
     a.status = nullptr;
+    a.claim = nullptr;
     a.mode = bcjr::kModeForward;
     a.kernel = bcjr::kKernelGeneric;
     a.grid = slots;

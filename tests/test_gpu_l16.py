@@ -68,6 +68,44 @@ def test_cluster_kernel_many_pairs_per_cluster(cuda_ok):
     np.testing.assert_array_equal(z_all[150:153], z_sub)
 
 
+def _run_env(env, w, cb, T, g):
+    saved = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        return _run(w, cb, T, g)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                del os.environ[k]
+            else:
+                os.environ[k] = v
+
+
+@pytest.mark.parametrize("B,N", [(301, 24), (160, 256), (75, 2)])
+def test_cluster_instances_agree_bitwise(cuda_ok, B, N):
+    """The 2-CTA and 4-CTA instances reduce per (1024-butterfly block, warp) in
+    one fixed order, so a sequence's soft codewords, log Z and gradient are
+    bitwise the same whichever instance runs it: forward on either instance,
+    backward on either alone and on both side by side (the default above one
+    round of the 2-CTA grid), where sequences go to whichever grid claims
+    them first."""
+    rng = np.random.default_rng(B * 1000 + N)
+    cb = rng.standard_normal((65536, 1)).astype(np.float32)
+    w = rng.standard_normal((B, N, 1)).astype(np.float32)
+    g = rng.standard_normal((B, N, 1)).astype(np.float32)
+    s2, z2, d2 = _run_env({"BCJR_B200_L16_FORWARD": "2", "BCJR_B200_L16_BACKWARD": "2"}, w, cb, 0.5, g)
+    s4, z4, d4 = _run_env({"BCJR_B200_L16_FORWARD": "4", "BCJR_B200_L16_BACKWARD": "4"}, w, cb, 0.5, g)
+    sd, zd, dd = _run_env({"BCJR_B200_L16_FORWARD": "0", "BCJR_B200_L16_BACKWARD": "0"}, w, cb, 0.5, g)
+    np.testing.assert_array_equal(s2, s4)
+    np.testing.assert_array_equal(z2, z4)
+    np.testing.assert_array_equal(d2, d4)
+    np.testing.assert_array_equal(s2, sd)
+    np.testing.assert_array_equal(d2, dd)
+    s64, z64, d64 = oracle.fb(w[:4], cb, 0.5, 16, 2, 1, grad_soft=g[:4])
+    np.testing.assert_allclose(s2[:4], s64, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(d2[:4], d64, rtol=1e-4, atol=1e-5)
+
+
 def test_low_temperature_normwise(cuda_ok):
     """T = 0.05 on random inputs.  Here the fp32 floor of the algorithm is at
     the elementwise tolerance (an fp32 emulation of these recursions reaches
@@ -114,3 +152,34 @@ def test_bounded_wait_timeout_is_reported_and_context_survives(cuda_ok):
     s1, _, _ = _run(w.cpu().numpy(), cb.cpu().numpy(), 0.5, np.ones((2, 8, 1), np.float32))
     s64, _, _ = oracle.fb(w.cpu().numpy(), cb.cpu().numpy(), 0.5, 16, 2, 1)
     np.testing.assert_allclose(s1, s64, rtol=1e-4, atol=1e-5)
+
+
+def test_bounded_wait_timeout_with_two_grids(cuda_ok):
+    """The same in the backward when the 4-CTA and 2-CTA grids run side by
+    side (B above one round of the 2-CTA grid): both grids stop at the
+    timeout, the status is reported, the context stays usable."""
+    from quant_2bit_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(5)
+    B, N = 160, 8
+    cb = torch.tensor(rng.standard_normal((65536, 1)), dtype=torch.float32, device=dev)
+    w = torch.tensor(rng.standard_normal((B, N, 1)), dtype=torch.float32, device=dev)
+    T = torch.tensor(0.5, device=dev)
+    soft = torch.rand_like(w)
+    g = torch.ones_like(w)
+    d = torch.empty_like(w)
+    ws = _lib.workspace(B, N, 16, 2, 1, _lib.WS_BACKWARD, dev)
+    P, sp = _lib.ptr, _lib.stream_ptr(dev)
+    os.environ["BCJR_B200_TEST_DROP_SENDS"] = "1"
+    try:
+        rc = lib.bcjr_fb_backward(P(w), P(cb), P(T), P(soft), P(g), B, N, 16, 2, 1, P(d),
+                                  P(ws), ws.numel(), sp)
+    finally:
+        del os.environ["BCJR_B200_TEST_DROP_SENDS"]
+    assert rc == 0
+    assert lib.bcjr_ws_status(P(ws), sp) == _lib.BCJR_ERR_TIMEOUT
+    wn = w[:3].cpu().numpy()
+    s1, _, d1 = _run(wn, cb.cpu().numpy(), 0.5, np.ones((3, N, 1), np.float32))
+    s64, _, d64 = oracle.fb(wn, cb.cpu().numpy(), 0.5, 16, 2, 1, grad_soft=np.ones((3, N, 1)))
+    np.testing.assert_allclose(d1, d64, rtol=1e-4, atol=1e-5)
