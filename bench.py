@@ -65,8 +65,8 @@ MUFU_PER_SM_CLK = 16
 # traffic grows in proportion to sequences.  V=1: L=16, N=256, 296 sequences
 # (2-CTA clusters); V=2: L=16, N=128, 297 sequences (part of the history rows
 # stays in L2).
-DRAM_BYTES_PER_SEQ = {1: {"forward": (4.822843e9 + 4.961722e9) / 296,
-                          "backward": (9.663011e9 + 9.910032e9) / 296},
+DRAM_BYTES_PER_SEQ = {1: {"forward": (4.812766e9 + 4.970556e9) / 296,
+                          "backward": (9.551417e9 + 9.918947e9) / 296},
                       2: {"forward": (0.364880e9 + 0.627745e9) / 297,
                           "backward": (0.998954e9 + 1.249169e9) / 297}}
 L2_BYTES = 126 * 1024 * 1024
