@@ -13,9 +13,9 @@
 // A_t(p 2^12 + j) and writes A_{t+1}(4 j + c); in the backward (beta)
 // direction it reads Bt_{t+1}(4 j + c) and writes Bt_t(p 2^12 + j).  Every
 // step touches the same 16 states per butterfly, so each thread owns
-// kJPT = 4 butterflies for the whole kernel and keeps their 64 codebook
-// values in registers: no codebook traffic after the first load.  CTA r of
-// the cluster owns butterflies [2048 r, 2048 r + 2048).
+// kJPT = 4 (2-CTA) or 2 (4-CTA) butterflies for the whole kernel and keeps
+// their codebook values in registers: no codebook traffic after the first
+// load.  CTA r of the cluster owns butterflies [r 4096/kCL, (r+1) 4096/kCL).
 //
 // Arithmetic
 // ----------
