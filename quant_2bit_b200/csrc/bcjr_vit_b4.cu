@@ -43,7 +43,10 @@ constexpr int kRPC = 64;              // butterflies per CTA
 constexpr int kIn = kRPC * 16;        // 1024 inputs per CTA per step
 constexpr int kNT = 512;
 constexpr int kWarps = kNT / 32;
-constexpr int kSlots = 2;
+#ifndef BCJR_VIT_SLOTS
+#define BCJR_VIT_SLOTS 2
+#endif
+constexpr int kSlots = BCJR_VIT_SLOTS;   // sequences in flight per cluster
 constexpr int kNMax = 512;
 
 struct alignas(128) Smem {

@@ -183,3 +183,18 @@ def test_bounded_wait_timeout_with_two_grids(cuda_ok):
     s1, _, d1 = _run(wn, cb.cpu().numpy(), 0.5, np.ones((3, N, 1), np.float32))
     s64, _, d64 = oracle.fb(wn, cb.cpu().numpy(), 0.5, 16, 2, 1, grad_soft=np.ones((3, N, 1)))
     np.testing.assert_allclose(d1, d64, rtol=1e-4, atol=1e-5)
+
+
+def test_kernel_launch_count(cuda_ok):
+    """bcjr_kernel_launches reports the grids a call launches: two for the
+    L=16, V=1 backward above one round of the 2-CTA grid (74 clusters of one
+    sequence on a B200), one otherwise."""
+    from quant_2bit_b200 import _lib
+    lib = _lib.load()
+    n = lambda B, V, flag: lib.bcjr_kernel_launches(B, 256 // V, 16, 2, V, flag)
+    assert n(4096, 1, _lib.WS_BACKWARD) == 2
+    assert n(74, 1, _lib.WS_BACKWARD) == 1
+    assert n(4096, 1, _lib.WS_FORWARD) == 1
+    assert n(4096, 2, _lib.WS_BACKWARD) == 1
+    assert n(0, 1, _lib.WS_BACKWARD) == 0
+    assert n(4096, 1, _lib.WS_FORWARD | _lib.WS_BACKWARD) == 0
