@@ -33,7 +33,7 @@ def _run(w, cb, T, grad, generic=False):
 
 
 @pytest.mark.parametrize("B,N,T", [(1, 2, 0.5), (3, 3, 1.0), (5, 17, 0.3), (2, 256, 0.1),
-                                   (77, 64, 0.5), (2, 512, 0.5), (1, 513, 0.5)])
+                                   (77, 64, 0.5), (2, 512, 0.5), (90, 512, 0.5), (1, 513, 0.5)])
 def test_cluster_kernel_vs_generic_and_oracle(cuda_ok, B, N, T):
     rng = np.random.default_rng(B * 1000 + N)
     cb = rng.standard_normal((65536, 1)).astype(np.float32)
@@ -81,7 +81,7 @@ def _run_env(env, w, cb, T, g):
                 os.environ[k] = v
 
 
-@pytest.mark.parametrize("B,N", [(301, 24), (160, 256), (75, 2)])
+@pytest.mark.parametrize("B,N", [(301, 24), (160, 256), (75, 2), (80, 512)])
 def test_cluster_instances_agree_bitwise(cuda_ok, B, N):
     """The 2-CTA and 4-CTA instances reduce per (1024-butterfly block, warp) in
     one fixed order, so a sequence's soft codewords, log Z and gradient are
