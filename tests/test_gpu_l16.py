@@ -2,6 +2,7 @@
 fp64 oracle and against the generic kernel on the same inputs, over ragged
 shapes (odd B leaves one cluster slot idle, B below the cluster count, the
 shortest and longest N it serves, and N beyond it, which falls back)."""
+import ctypes
 import os
 
 import numpy as np
@@ -198,3 +199,56 @@ def test_kernel_launch_count(cuda_ok):
     assert n(4096, 2, _lib.WS_BACKWARD) == 1
     assert n(0, 1, _lib.WS_BACKWARD) == 0
     assert n(4096, 1, _lib.WS_FORWARD | _lib.WS_BACKWARD) == 0
+
+
+def test_graph_capture_replays_forward_and_backward(cuda_ok):
+    """Forward + backward captured in one CUDA graph through the C ABI (the
+    backward with its two grids, B above one round of the 2-CTA grid) replay
+    bitwise like eager calls, also after the inputs change in place."""
+    from quant_2bit_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(31)
+    B, N = 160, 32
+    cb = torch.tensor(rng.standard_normal((65536, 1)), dtype=torch.float32, device=dev)
+    w = torch.tensor(rng.standard_normal((B, N, 1)), dtype=torch.float32, device=dev)
+    g = torch.tensor(rng.standard_normal((B, N, 1)), dtype=torch.float32, device=dev)
+    T = torch.tensor(0.5, device=dev)
+    soft, logZ, d = torch.empty_like(w), torch.empty(B, device=dev), torch.empty_like(w)
+    ws_f = _lib.workspace(B, N, 16, 2, 1, _lib.WS_FORWARD, dev)
+    ws_b = _lib.workspace(B, N, 16, 2, 1, _lib.WS_BACKWARD, dev)
+    assert lib.bcjr_kernel_launches(B, N, 16, 2, 1, _lib.WS_BACKWARD) == 2
+    P = _lib.ptr
+
+    def calls(stream):
+        sp = ctypes.c_void_p(stream.cuda_stream)
+        assert lib.bcjr_fb_forward(P(w), P(cb), P(T), B, N, 16, 2, 1, P(soft), P(logZ),
+                                   P(ws_f), ws_f.numel(), sp) == 0
+        assert lib.bcjr_fb_backward(P(w), P(cb), P(T), P(soft), P(g), B, N, 16, 2, 1, P(d),
+                                    P(ws_b), ws_b.numel(), sp) == 0
+
+    def eager():
+        calls(torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        return soft.clone(), logZ.clone(), d.clone()
+
+    ref = eager()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(graph, stream=side):
+        calls(side)
+    for x in (soft, logZ, d):
+        x.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, b in zip((soft, logZ, d), ref):
+        assert torch.equal(a, b)
+    w.copy_(torch.tensor(rng.standard_normal((B, N, 1)), dtype=torch.float32, device=dev))
+    graph.replay()
+    torch.cuda.synchronize()
+    got = (soft.clone(), logZ.clone(), d.clone())
+    want = eager()
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
+    del graph
