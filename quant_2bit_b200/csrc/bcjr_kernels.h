@@ -64,6 +64,6 @@ bool vit_b4_applicable(int N, int L, int k, int V, const void *cb);
 size_t vit_b4_workspace_bytes(int B, int N);
 cudaError_t launch_vit_b4(const float *seq, const float *cb, int B, int N, int *bits,
                           int *starts, float *recon, float *mse, void *ws, size_t ws_bytes,
-                          int *status, cudaStream_t st);
+                          int *status, int drop_sends, cudaStream_t st);
 
 }  // namespace bcjr

@@ -71,7 +71,8 @@ __device__ __forceinline__ void arg_better(float &v, int &i, float v2, int i2) {
 
 __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(kNT, 1)
 vit_b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B, int N,
-              unsigned char *__restrict__ bp_all, int *__restrict__ final_states, int *status) {
+              unsigned char *__restrict__ bp_all, int *__restrict__ final_states, int *status,
+              int drop_sends) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
     constexpr uint32_t kBytes = kIn * 4 + kCL * kWarps * 4;
@@ -118,6 +119,9 @@ vit_b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
     cluster_sync();
 
     bool failed = false;
+    // Test-only fault injection (BCJR_B200_TEST_DROP_SENDS): CTA rank 1 never
+    // sends its group minima or tokens, so every consumer's bounded wait expires.
+    const bool drop = drop_sends != 0 && rank == 1;
     uint32_t use[kSlots];
 #pragma unroll
     for (int z = 0; z < kSlots; ++z) use[z] = 0;
@@ -195,7 +199,7 @@ vit_b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
                         }
                     }
                 }
-                if (!last && !failed) {
+                if (!last && !failed && !drop) {
                     const uint32_t bar = a_base + soff(&sm.full[z][nb]);
                     st_async2(a_base + soff(&sm.buf[z][nb][0]) + 4u * a_off, o[0], o[1], bar);
                     __syncwarp();
@@ -256,7 +260,10 @@ __global__ void vit_b4_backtrace(const unsigned char *__restrict__ bp_all,
                                  float *__restrict__ recon, float *__restrict__ mse) {
     const long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
-    int s = final_states[b];
+    // The masks keep every index in range whatever the arrays hold: after a
+    // wait timeout (BCJR_ERR_TIMEOUT) the forward kernel leaves backpointers
+    // and final states unwritten, and this walk must still read in bounds.
+    int s = final_states[b] & ((1 << kL) - 1);
     double e2 = 0.0;
     for (int t = N - 1; t >= 0; --t) {
         const long i = b * N + t;
@@ -268,7 +275,7 @@ __global__ void vit_b4_backtrace(const unsigned char *__restrict__ bp_all,
         const double d1 = (double)r1 - (double)__ldg(seq + 2 * i + 1);
         e2 += d0 * d0 + d1 * d1;
         const int h = s >> 4;
-        if (t > 0) s = ((int)bp_all[((size_t)b * N + t) * kG + h] << 12) | h;
+        if (t > 0) s = (((int)bp_all[((size_t)b * N + t) * kG + h] & 15) << 12) | h;
         else s = h;   // step 0's backpointers are all 0
     }
     starts[b] = s;
@@ -328,7 +335,7 @@ size_t vit_b4_workspace_bytes(int B, int N) {
 
 cudaError_t launch_vit_b4(const float *seq, const float *cb, int B, int N, int *bits,
                           int *starts, float *recon, float *mse, void *ws, size_t ws_bytes,
-                          int *status, cudaStream_t st) {
+                          int *status, int drop_sends, cudaStream_t st) {
     const long c = B < kVitChunk ? B : kVitChunk;
     unsigned char *bp = static_cast<unsigned char *>(ws) + 256;
     int *finals = reinterpret_cast<int *>(bp + (size_t)c * N * vb4::kG);
@@ -340,7 +347,7 @@ cudaError_t launch_vit_b4(const float *seq, const float *cb, int B, int N, int *
         long ncl = (nb + vb4::kSlots - 1) / vb4::kSlots;
         if (ncl > maxc) ncl = maxc;
         vb4::vit_b4_kernel<<<(unsigned)(ncl * vb4::kCL), vb4::kNT, sizeof(vb4::Smem), st>>>(
-            seq + b0 * N * 2, cb, nb, N, bp, finals, status);
+            seq + b0 * N * 2, cb, nb, N, bp, finals, status, drop_sends);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         vb4::vit_b4_backtrace<<<(nb + 127) / 128, 128, 0, st>>>(

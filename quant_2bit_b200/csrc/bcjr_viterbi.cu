@@ -244,8 +244,12 @@ BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L
     const size_t data_bytes = ws_bytes - kVitHeader;
     if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return BCJR_ERR_LAUNCH;
     if (vit_use_cluster(N, L, k, V, cb) && data_bytes >= bcjr::vit_b4_workspace_bytes(B, N)) {
+        // Test-only: BCJR_B200_TEST_DROP_SENDS=1 makes the cluster kernel's CTA 1
+        // withhold its outputs so that the bounded waits time out (tests/ only).
+        const char *drop = std::getenv("BCJR_B200_TEST_DROP_SENDS");
         const cudaError_t e = bcjr::launch_vit_b4(seq, cb, B, N, bitstreams, start_states, recons,
-                                                  mses, data, data_bytes, status, s);
+                                                  mses, data, data_bytes, status,
+                                                  (drop && drop[0] == '1') ? 1 : 0, s);
         return e == cudaSuccess ? BCJR_OK : BCJR_ERR_LAUNCH;
     }
     const size_t slot = bcjr::vit::slot_bytes(N, L, k * V);

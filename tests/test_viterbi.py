@@ -116,3 +116,40 @@ def test_cluster_and_generic_kernels_agree(cuda_ok, B, N):
     for x, y in zip(a[:3], b[:3]):
         assert torch.equal(x, y)
     torch.testing.assert_close(a[3], b[3], rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.gpu
+def test_cluster_wait_timeout_is_reported_and_context_survives(cuda_ok):
+    """Failure detection without a GPU fault: with BCJR_B200_TEST_DROP_SENDS=1
+    one CTA of each cluster withholds its group minima, every bounded wait of
+    the cluster Viterbi expires (~1 s), the status word reports
+    BCJR_ERR_TIMEOUT, the walk-back still reads in bounds, and the next
+    normal call on the same context is bit-exact."""
+    import os
+    from quant_2bit_b200 import _lib
+    from quant_2bit_b200.viterbi import viterbi_encode_batched
+    lib = _lib.load()
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(17)
+    B, N = 8, 16
+    cb = torch.tensor(hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32)), device=dev)
+    seqs = torch.tensor(rng.standard_normal((B, 2 * N)).astype(np.float32), device=dev)
+    bits = torch.empty((B, N), dtype=torch.int32, device=dev)
+    starts = torch.empty((B,), dtype=torch.int32, device=dev)
+    rec = torch.empty((B, 2 * N), dtype=torch.float32, device=dev)
+    mse = torch.empty((B,), dtype=torch.float32, device=dev)
+    ws = torch.empty(lib.bcjr_viterbi_workspace_bytes(B, N, 16, 2, 2), dtype=torch.uint8, device=dev)
+    P, sp = _lib.ptr, _lib.stream_ptr(dev)
+    os.environ["BCJR_B200_TEST_DROP_SENDS"] = "1"
+    try:
+        rc = lib.bcjr_viterbi(P(seqs), P(cb), B, N, 16, 2, 2, P(bits), P(starts), P(rec), P(mse),
+                              P(ws), ws.numel(), sp)
+    finally:
+        del os.environ["BCJR_B200_TEST_DROP_SENDS"]
+    assert rc == 0
+    assert lib.bcjr_ws_status(P(ws), sp) == _lib.BCJR_ERR_TIMEOUT
+    assert int(starts.max()) < 65536 and int(bits.max()) < 16
+    out = [o.cpu().numpy() for o in viterbi_encode_batched(seqs, cb, 16, 2, 2)]
+    ref = viterbi.viterbi(seqs.cpu().numpy(), cb.cpu().numpy(), 16, 2, 2)
+    for a, b in zip(out[:3], ref[:3]):
+        np.testing.assert_array_equal(a, b)
