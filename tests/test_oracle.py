@@ -102,6 +102,25 @@ def test_high_temperature_limit_is_codebook_mean():
     np.testing.assert_allclose(soft[0, :, 0], np.full(8, cb.mean()), atol=1e-5)
 
 
+@pytest.mark.parametrize("L,k,V", [(6, 2, 1), (8, 2, 2), (6, 1, 2)])
+def test_low_temperature_limit_is_the_viterbi_walk(L, k, V):
+    """T -> 0: the posterior concentrates on the minimum-cost walk, so the soft
+    codewords approach the hard Viterbi reconstruction and -T log Z approaches
+    that walk's cost (src/bcjr/forward_backward.py:37-38); the two oracles are
+    independent restatements (sum-product in fp64, exact min-sum)."""
+    from oracle import viterbi
+    rng = np.random.default_rng(L * 10 + V)
+    cb = rng.standard_normal((1 << L, V))
+    w = rng.standard_normal((3, 12, V))
+    T = 1e-5
+    soft, logZ, _ = oracle.fb(w, cb, T, L, k, V)
+    _, _, rec, mse = viterbi.viterbi(w.reshape(3, -1).astype(np.float32),
+                                     cb.astype(np.float32), L, k, V)
+    np.testing.assert_allclose(soft.reshape(3, -1), rec, atol=1e-5)
+    cost = mse.astype(np.float64) * 12 * V
+    np.testing.assert_allclose(-T * logZ, cost, rtol=1e-5, atol=1e-4)
+
+
 def test_shift_invariance_of_soft():
     """Shifting the codebook and the weights by the same constant leaves every
     |c - w| unchanged: log Z is unchanged and soft shifts by the constant."""
