@@ -4,16 +4,19 @@
                     [--config c2|c3|c5|v2|layer|viterbi] [--temperature T] [--weights gauss|t3]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, NCCL)
 
-Workload (synthetic, seeded): L=16, k=2, V=1, N=256 steps,
-T=0.5, codebook randn(65536) (seed 0), weights randn drawn after the codebook.
-* c2 (default): one 1024x1024 weight = 4,096 sequences per GPU (weak scaling:
-  every rank quantizes its own matrix; the soft matrices are all-gathered
-  over NCCL when N > 1).
-* c3: the Llama-3.2-1B-shaped layer (237,568 sequences, per-row scale
-  U[0.5,2]) sharded across the N ranks (strong scaling), soft weights
-  all-gathered.
-* c5: the OLMoE-shaped MoE layer (1,572,864 sequences), experts sharded
-  8 per GPU at N=8 (strong scaling).
+Workload (synthetic, seeded): L=16, k=2, V=1, N=256 steps, T=0.5, codebook
+randn(65536) (seed 0), weights randn drawn after the codebook.
+* c3 (default): the Llama-3.2-1B-shaped decoder layer, q/o 2048x2048, k/v
+  512x2048, gate/up 8192x2048, down 2048x8192 (237,568 sequences, per-row
+  scale U[0.5,2]), tile-sharded across the N ranks (strong scaling) through
+  quant_2bit_b200.distributed: one forward launch per weight, each weight's
+  soft matrix all-gathered over NCCL on a side stream while the next
+  weight's kernels run.
+* c2: one 1024x1024 weight = 4,096 sequences per GPU (weak scaling: one
+  weight of 4,096 N tiles split over the ranks and all-gathered).
+* c5: the OLMoE-shaped MoE layer (64 experts x gate/up 1024x2048, down
+  2048x1024; 1,572,864 sequences, per-expert scale U[0.5,2]), whole experts
+  per GPU (64 / N each, strong scaling; nothing to reassemble).
 * v2: the shape the reference's QAT layers use, k=2, V=2 (b = 4, 16
   predecessors per state), N=128: one 1024x1024 weight = 4,096 sequences of
   128 two-dimensional steps per GPU, codebook randn(65536, 2).
@@ -27,8 +30,16 @@ T=0.5, codebook randn(65536) (seed 0), weights randn drawn after the codebook.
   viterbi_encode_v_batched_cuda; its own metric (min-sum transitions/s).
 
 One step = forward (soft) + backward (d_seq for an upstream gradient of ones)
-of every local sequence (+ the all-gather when N > 1).  One transition = one
-trellis edge: B * N * 2^L * 2^kV per step.
+of every local sequence (+ the per-weight all-gathers when N > 1; the
+backward runs on each rank's own tiles, whose latent weights it owns, with
+that rank's rows of the upstream gradient).  One transition = one trellis
+edge: B * N * 2^L * 2^kV per step.
+
+--impl reference: the reference's own eager torch BCJR
+(src.bcjr.forward_backward.bcjr_forward_backward, imported unmodified from
+baseline/_ref when that install is present, else its restatement
+oracle/torch_port.py) on the host's CPU cores, on a bounded sample of the
+same workload per step.
 """
 import argparse
 import json
@@ -79,7 +90,29 @@ def llama_layer_shapes():
 
 
 def olmoe_layer_shapes():
+    # gate, up, down of each of the 64 experts
     return [(1024, 2048), (1024, 2048), (2048, 1024)] * 64
+
+
+def layer_shapes(config):
+    return llama_layer_shapes() if config in ("c3", "layer") else olmoe_layer_shapes()
+
+
+def layer_matrix(config, idx):
+    """Weight `idx` of a layer workload and its scale, on CPU.
+
+    c3 / layer: the Llama-3.2-1B layer, randn(m, n) times a per-row scale
+    U[0.5, 2] (scale drawn first from the matrix's generator, then W).
+    c5: the OLMoE layer, randn(m, n) times one scale U[0.5, 2] per expert,
+    shared by the expert's gate, up and down weights (matrices 3e .. 3e+2)."""
+    m, n = layer_shapes(config)[idx]
+    gm = torch.Generator().manual_seed(100 + idx)
+    if config in ("c3", "layer"):
+        scale = torch.empty(m, 1).uniform_(0.5, 2.0, generator=gm)
+    else:
+        ge = torch.Generator().manual_seed(5000 + idx // 3)
+        scale = torch.empty(1, 1).uniform_(0.5, 2.0, generator=ge)
+    return torch.randn(m, n, generator=gm) * scale, scale
 
 
 def tile(W, Tx=16, Ty=16):
@@ -89,10 +122,24 @@ def tile(W, Tx=16, Ty=16):
     return W.view(m, n // Ty, Ty).permute(1, 0, 2).reshape((m // Tx) * (n // Ty), Tx * Ty)
 
 
+def layer_plan(config, world, rank):
+    """How a layer workload is split over the ranks (quant_2bit_b200.distributed.LayerShards):
+    c3 splits every weight's tiles evenly; c5 keeps each expert's three
+    weights on one rank (64 / world experts per rank)."""
+    from quant_2bit_b200.distributed import LayerShards
+    counts = [(m // 16) * (n // 16) for m, n in layer_shapes(config)]
+    if config == "c5":
+        return LayerShards(counts, world, rank, owners=[(i // 3) * world // 64 for i in range(len(counts))])
+    return LayerShards(counts, world, rank)
+
+
 def make_inputs(config, rank, world, weights="gauss"):
-    """Codebook (65536, V) and this rank's sequences (B_local, N, V), on CPU.
-    weights="t3": config 4's heavy-tailed variant, Student-t(3)/sqrt(3) drawn
-    with numpy.random.default_rng(seed) in place of the N(0,1) draws."""
+    """Codebook (65536, V) and this rank's sequences (B_local, N, V), on CPU,
+    and the total sequence count of the job.  For the layer workloads the
+    local sequences are this rank's share of every weight (layer_plan), in
+    weight order.  weights="t3": config 4's heavy-tailed variant,
+    Student-t(3)/sqrt(3) drawn with numpy.random.default_rng(seed) in place of
+    the N(0,1) draws."""
     V, NSTEP = SHAPES[config]
     g = torch.Generator().manual_seed(0)
     cb = torch.randn(1 << L, V, generator=g)
@@ -103,26 +150,14 @@ def make_inputs(config, rank, world, weights="gauss"):
             w = torch.tensor(np.random.default_rng(rank).standard_t(3, size=(4096, NSTEP, V))
                              / math.sqrt(3.0), dtype=torch.float32)
         return cb, w, 4096 * world
-    shapes = llama_layer_shapes() if config in ("c3", "layer") else olmoe_layer_shapes()
-    total = sum((m // 16) * (n // 16) for m, n in shapes)
-    lo, hi = rank * total // world, (rank + 1) * total // world
-    seqs, off = [], 0
-    gs = torch.Generator().manual_seed(7)
-    for idx, (m, n) in enumerate(shapes):
-        cnt = (m // 16) * (n // 16)
-        if off + cnt > lo and off < hi:
-            gm = torch.Generator().manual_seed(100 + idx)
-            if config in ("c3", "layer"):
-                scale = torch.empty(m, 1).uniform_(0.5, 2.0, generator=gm)
-            else:
-                scale = torch.empty(1, 1).uniform_(0.5, 2.0, generator=gm)
-            W = torch.randn(m, n, generator=gm) * scale
-            t = tile(W)
-            a, b_ = max(lo, off) - off, min(hi, off + cnt) - off
-            seqs.append(t[a:b_])
-        off += cnt
+    plan = layer_plan(config, world, rank)
+    seqs = []
+    for idx, (lo, hi) in enumerate(plan.ranges):
+        if hi > lo:
+            W, _ = layer_matrix(config, idx)
+            seqs.append(tile(W)[lo:hi])
     w = torch.cat(seqs).view(-1, NSTEP, V).contiguous()
-    return cb, w, total
+    return cb, w, plan.total
 
 
 class ClockSampler:
@@ -177,32 +212,94 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_reference(args, rank):
-    """The reference's eager torch BCJR (restated in oracle/torch_port.py) on
-    the host's CPU cores: one forward + backward of a bounded sample of the
-    same workload per step."""
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def reference_fb():
+    """(fn(seq, cb, T, V) -> None running forward + backward with an
+    upstream gradient of ones, kind).  The reference's own eager
+    bcjr_forward_backward (src/bcjr/forward_backward.py:190-232), imported
+    unmodified from its install in baseline/_ref; without that install, its
+    restatement oracle/torch_port.py (bitwise equal on CPU)."""
+    if os.path.isdir(os.path.join(REF_DIR, "src", "bcjr")):
+        sys.path.insert(0, REF_DIR)
+        try:
+            from src.bcjr.forward_backward import bcjr_forward_backward as ref
+        finally:
+            sys.path.remove(REF_DIR)
+
+        def run(seq, cb, T, V):
+            x = seq.detach().clone().requires_grad_(True)
+            soft, _ = ref(x, cb, float(T), L=L, k=K_BITS, V=V)
+            soft.sum().backward()
+        return run, "reference"
+    from oracle import torch_port
+
+    def run(seq, cb, T, V):
+        torch_port.fwd_bwd(seq, cb, T, L, K_BITS, V, chunk=8)
+    return run, "port"
+
+
+def cpu_sample(config, nseq, weights="gauss"):
+    """The first `nseq` sequences of the workload (per-sequence cost does not
+    depend on the data) and the codebook, on CPU."""
+    V, NSTEP = SHAPES[config]
+    g = torch.Generator().manual_seed(0)
+    cb = torch.randn(1 << L, V, generator=g)
+    if config in ("c3", "c5", "layer"):
+        w = tile(layer_matrix(config, 0)[0])[:nseq].reshape(nseq, NSTEP, V).contiguous()
+    else:
+        w = make_inputs(config, 0, 1, weights)[1][:nseq].contiguous()
+    return cb, w
+
+
+def cpu_reference(args, nseq, steps, warmup):
+    """The reference's eager torch BCJR on all the host's CPU cores, in
+    chunks of 8 sequences (the reference default BCJR_CHUNK=8,
+    src/bcjr/bcjr_quant.py:60): `warmup` untimed steps, then `steps` timed
+    steps, each one forward + backward (upstream gradient of ones) of the
+    same `nseq`-sequence sample of the workload."""
     if args.config == "viterbi":
         return cpu_viterbi(args)
-    from oracle import torch_port
     V, NSTEP = SHAPES[args.config]
     edges_per_seq = NSTEP * (1 << L) * (1 << (K_BITS * V))
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cb, w, _ = make_inputs(args.config, 0, 1, args.weights)
-    nseq = args.cpu_sample_seqs
-    sample = w[:nseq]
-    for _ in range(args.warmup if args.impl == "reference" else 0):
-        torch_port.fwd_bwd(sample, cb, args.temperature, L, K_BITS, V, chunk=8)
+    run, kind = reference_fb()
+    cb, sample = cpu_sample(args.config, nseq, args.weights)
+
+    def one_step(x):
+        for i in range(0, x.shape[0], 8):
+            run(x[i:i + 8], cb, args.temperature, V)
+
+    warm = sample[:1] if steps == 1 else sample     # a single timed step: a 1-sequence warm-up
+    for _ in range(warmup):
+        one_step(warm)
     t0 = time.perf_counter()
-    steps = args.steps if args.impl == "reference" else 1
     for _ in range(steps):
-        torch_port.fwd_bwd(sample, cb, args.temperature, L, K_BITS, V, chunk=8)
+        one_step(sample)
     dt = (time.perf_counter() - t0) / steps
     value = nseq * edges_per_seq / dt
-    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{nseq} sequence(s) of {args.config} (L=16, V={V}, N={NSTEP}), fwd + bwd with "
-                      f"grad=ones, chunk 8, torch {torch.__version__} CPU, "
-                      f"{threads} threads, {dt:.2f} s per step"}
+    what = ("the reference's src.bcjr.forward_backward.bcjr_forward_backward (unmodified, "
+            "baseline/_ref)" if kind == "reference" else
+            "oracle/torch_port.py (the reference's eager ops restated; baseline/_ref absent)")
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "cpu": cpu_model(),
+            "sample_sequences": nseq,
+            "sample": f"{nseq} sequence(s) of {args.config} (L=16, k=2, V={V}, N={NSTEP}, "
+                      f"T={args.temperature:g}), fwd + bwd with grad=ones, chunks of 8, {what}, "
+                      f"torch {torch.__version__} CPU, {threads} threads, {warmup} warm-up "
+                      f"step(s), {dt:.2f} s per timed step"}
 
 
 def hbm_peak_gbs():
@@ -459,64 +556,25 @@ def run_viterbi(args, rank, world, local_rank):
     print(json.dumps(result), flush=True)
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c5", "v2", "layer", "viterbi"])
-    ap.add_argument("--temperature", type=float, default=TEMP,
-                    help="T (config 4 sweeps 4, 2, 1, 0.5, 0.25, 0.1, 0.05)")
-    ap.add_argument("--weights", default="gauss", choices=["gauss", "t3"],
-                    help="config 4's Student-t(3) weights with --config c2")
-    ap.add_argument("--cpu-sample-seqs", type=int, default=1)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--sequences", type=int, default=0,
-                    help="use only this many sequences per GPU (small cases for ncu)")
-    ap.add_argument("--no-e2e", action="store_true")
-    args = ap.parse_args()
+# FMA-pipe busy cycles per state-step (SM-cycles) of the cluster kernels,
+# measured by ncu (sm__pipe_fma_cycles_active.sum over one launch / the
+# launch's state-steps; profiles/): the basis of the FP32-issue fraction in
+# the bench line, next to the MUFU fraction.
+FMA_CYCLES_PER_STATE_STEP = {1: {"forward": 0.0956, "backward": 0.1985},
+                             2: {"forward": None, "backward": None}}
+
+
+def run_bcjr(args, rank, world, local_rank):
+    """Configs c2 / c3 / c5 / v2: forward + backward of every sequence
+    through quant_2bit_b200.distributed (the product's sharding API)."""
+    import quant_2bit_b200 as q
+    from quant_2bit_b200 import _lib
+    from quant_2bit_b200 import distributed as qd
 
     V, NSTEP = SHAPES[args.config]
     EDGES_PER_SEQ = NSTEP * (1 << L) * (1 << (K_BITS * V))
     STATE_STEPS_PER_SEQ = NSTEP * (1 << L)
     MUFU_FWD, MUFU_BWD = MUFU[V]
-    weak = args.config in ("c2", "v2")
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        ref = cpu_reference(args, rank)
-        nsample = ref.get("sample_sequences", args.cpu_sample_seqs)
-        line = {"metric": VITERBI_METRIC if args.config == "viterbi" else METRIC,
-                "value": ref["value"], "unit": UNIT, "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": nsample * EDGES_PER_SEQ / ref["value"] * 1e3,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f32", "data": "synthetic (seeded randn, BASELINE configs)",
-                "impl": "reference",
-                "config": {"workload": f"{args.config}: L=16 k=2 V={V} N={NSTEP} T={args.temperature:g} "
-                                       f"{args.weights} weights, CPU sample",
-                           "sample_sequences": nsample},
-                "cpu_baseline": ref,
-                "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
-        return
-
-    if args.config == "layer":
-        run_layer(args, rank, world, local_rank)
-        return
-    if args.config == "viterbi":
-        run_viterbi(args, rank, world, local_rank)
-        return
-
-    import quant_2bit_b200 as q
-    from quant_2bit_b200 import _lib
-
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
@@ -524,47 +582,39 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
     cb_cpu, w_cpu, total_seqs = make_inputs(args.config, rank, world, args.weights)
-    if args.sequences:
-        w_cpu = w_cpu[:args.sequences].contiguous()
-        total_seqs = w_cpu.shape[0] * world
+    if args.config in ("c3", "c5") and not args.sequences:
+        shards = layer_plan(args.config, world, rank)
+    else:
+        if args.sequences:
+            w_cpu = w_cpu[:args.sequences].contiguous()
+        # one weight of (local sequences x world) tiles, split evenly
+        shards = qd.LayerShards([w_cpu.shape[0] * world], world, rank)
+        total_seqs = shards.total
+    assert shards.local == w_cpu.shape[0]
     cb = cb_cpu.to(dev)
     w = w_cpu.to(dev)
     Bl = w.shape[0]
     T = torch.tensor(args.temperature, dtype=torch.float32, device=dev)
-    soft = torch.empty((Bl, NSTEP, V), device=dev)
-    logZ = torch.empty((Bl,), device=dev)
     grad = torch.ones((Bl, NSTEP, V), device=dev)
-    dseq = torch.empty_like(soft)
-    lib = _lib.load()
-    ws_f = _lib.workspace(Bl, NSTEP, L, K_BITS, V, _lib.WS_FORWARD, dev)
-    ws_b = _lib.workspace(Bl, NSTEP, L, K_BITS, V, _lib.WS_BACKWARD, dev)
-    gathered = torch.empty((Bl * world, NSTEP, V), device=dev) if world > 1 else None
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    sp = _lib.stream_ptr(dev)
+    lib = _lib.load()
+    gather = world > 1 and shards.split
+    last = {}
 
-    def fwd():
-        _lib.check(lib.bcjr_fb_forward(_lib.ptr(w), _lib.ptr(cb), _lib.ptr(T), Bl, NSTEP, L,
-                                       K_BITS, V, _lib.ptr(soft), _lib.ptr(logZ),
-                                       _lib.ptr(ws_f), ws_f.numel(), sp), "forward")
-
-    def bwd():
-        _lib.check(lib.bcjr_fb_backward(_lib.ptr(w), _lib.ptr(cb), _lib.ptr(T), _lib.ptr(soft),
-                                        _lib.ptr(grad), Bl, NSTEP, L, K_BITS, V,
-                                        _lib.ptr(dseq), _lib.ptr(ws_b), ws_b.numel(), sp),
-                   "backward")
-
-    def step(ev=None):
+    def step(ev=None, do_gather=gather):
         if ev:
             ev[0].record(stream)
-        fwd()
+        soft, handle = qd.layer_forward(w, shards, cb, T, L, K_BITS, V, gather=do_gather)
         if ev:
             ev[1].record(stream)
-        bwd()
+        d = qd.layer_backward(w, soft, grad, cb, T, L, K_BITS, V)
         if ev:
             ev[2].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, soft)
+        handle.wait()
+        if ev:
+            ev[3].record(stream)
+        last["soft"], last["d"] = soft, d
 
     for _ in range(args.warmup):
         step()
@@ -582,52 +632,71 @@ def main():
     for i in range(args.steps):
         flush.zero_()                     # L2 flush between timed steps (outside the events)
         step(events[i])
-        events[i][3].record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
+    # a failed bounded wait turns the outputs of the call into NaN: a number
+    # timed over failed calls is not reported
+    bad = (~torch.isfinite(last["soft"])).any() | (~torch.isfinite(last["d"])).any()
+    nbad = torch.tensor([float(bad)], dtype=torch.float64, device=dev)
 
-    # kernels of one forward + backward call pair (the backward of L=16, V=1
-    # runs two grids side by side above one round of the 2-CTA grid)
-    launches_per_step = (lib.bcjr_kernel_launches(Bl, NSTEP, L, K_BITS, V, _lib.WS_FORWARD) +
-                         lib.bcjr_kernel_launches(Bl, NSTEP, L, K_BITS, V, _lib.WS_BACKWARD))
     step_ms = [e[0].elapsed_time(e[3]) for e in events]
     fwd_ms = [e[0].elapsed_time(e[1]) for e in events]
     bwd_ms = [e[1].elapsed_time(e[2]) for e in events]
-    t_local = sum(step_ms)
-    t = torch.tensor([t_local], dtype=torch.float64, device=dev)
+    tail_ms = [e[2].elapsed_time(e[3]) for e in events]
+    t = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(nbad, op=dist.ReduceOp.MAX)
     t_max_ms = float(t.item())
-    edges_total = (Bl * world if weak or args.sequences else total_seqs) * EDGES_PER_SEQ
+    edges_total = total_seqs * EDGES_PER_SEQ
     value = edges_total * args.steps / (t_max_ms / 1e3)
 
-    # e2e: the public autograd API with host buffers, H2D and D2H in the timed region.
+    # the same step without the all-gathers: what the collectives cost
+    t_nogather = None
+    if gather:
+        nsteps = min(args.steps, 3)
+        ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nsteps)]
+        dist.barrier()
+        for i in range(nsteps):
+            flush.zero_()
+            step(ev2[i], do_gather=False)
+        torch.cuda.synchronize()
+        tn = torch.tensor([sum(e[0].elapsed_time(e[3]) for e in ev2) / nsteps],
+                          dtype=torch.float64, device=dev)
+        dist.all_reduce(tn, op=dist.ReduceOp.MAX)
+        t_nogather = float(tn.item())
+
+    # e2e: the public autograd API (quant_2bit_b200.distributed.sharded_bcjr_layer)
+    # with this rank's weights in pinned host memory: H2D of the weights, the
+    # per-weight soft matrices (all-gathered), backward with an upstream
+    # gradient of ones, D2H of this rank's soft rows and gradient.
     w_host = w_cpu.pin_memory()
     soft_host = torch.empty((Bl, NSTEP, V)).pin_memory()
     dseq_host = torch.empty((Bl, NSTEP, V)).pin_memory()
+    e2e_steps = min(args.steps, 3)
 
     def e2e_step():
         x = w_host.to(dev, non_blocking=True).requires_grad_(True)
-        s, _ = q.bcjr_forward_backward(x, cb, T, L=L, k=K_BITS, V=V)
-        s.sum().backward()
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, s.detach())
-        soft_host.copy_(s.detach(), non_blocking=True)
+        outs = qd.sharded_bcjr_layer(x, cb, T, shards, L, K_BITS, V, grad_reduce=False)
+        torch.autograd.backward([o for o in outs if o.shape[0]],
+                                [torch.ones_like(o) for o in outs if o.shape[0]])
+        rows = [o[lo:hi] if shards.split else o for o, (lo, hi) in zip(outs, shards.ranges)
+                if hi > lo]
+        soft_host.copy_(torch.cat(rows) if len(rows) > 1 else rows[0], non_blocking=True)
         dseq_host.copy_(x.grad, non_blocking=True)
 
     e2e_value = None
     if not args.no_e2e:
-        for _ in range(max(1, args.warmup // 2)):
-            e2e_step()
+        e2e_step()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(e2e_steps):
             e2e_step()
         e1.record(stream)
         torch.cuda.synchronize()
@@ -635,61 +704,151 @@ def main():
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
             dist.barrier()
-        e2e_value = edges_total * args.steps / (float(te.item()) / 1e3)
+        e2e_value = edges_total * e2e_steps / (float(te.item()) / 1e3)
 
     # roofline of the dominant kernel (MUFU-bound; algorithmic ops per launch)
     fwd_avg = sum(fwd_ms) / len(fwd_ms)
     bwd_avg = sum(bwd_ms) / len(bwd_ms)
     sstep = Bl * STATE_STEPS_PER_SEQ
-    if bwd_avg >= fwd_avg:
-        dom, dom_ms, ops = "backward", bwd_avg, MUFU_BWD * sstep
-    else:
-        dom, dom_ms, ops = "forward", fwd_avg, MUFU_FWD * sstep
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    dom, dom_ms, ops = (("backward", bwd_avg, MUFU_BWD * sstep) if bwd_avg >= fwd_avg
+                        else ("forward", fwd_avg, MUFU_FWD * sstep))
+    sms = props.multi_processor_count
     clk_mhz = clk.get("sm_max_mhz") or 1965.0
     peak = sms * MUFU_PER_SM_CLK * clk_mhz * 1e6 / 1e9          # Gop/s at max SM clock
     achieved = ops / (dom_ms / 1e3) / 1e9
-
+    fma = FMA_CYCLES_PER_STATE_STEP[V][dom]
+    fp32 = None
+    if fma is not None:
+        fp32 = {"frac": fma * sstep / (dom_ms / 1e3 * clk_mhz * 1e6 * sms),
+                "basis": f"{fma} FMA-pipe busy SM-cycles per state-step (ncu "
+                         "sm__pipe_fma_cycles_active, profiles/) x state-steps / "
+                         f"(kernel time x {clk_mhz:.0f} MHz x {sms} SMs)"}
+    # our kernels per step: one forward call per weight when gathering (else
+    # one), one backward call; a call's grids from bcjr_kernel_launches
+    n_fwd = len([1 for lo, hi in shards.ranges if hi > lo]) if gather else 1
+    launches_per_step = (n_fwd * lib.bcjr_kernel_launches(Bl, NSTEP, L, K_BITS, V, _lib.WS_FORWARD)
+                         + lib.bcjr_kernel_launches(Bl, NSTEP, L, K_BITS, V, _lib.WS_BACKWARD))
+    names = {"c2": "config 2: one 1024x1024 weight per GPU",
+             "c3": "config 3: Llama-3.2-1B decoder layer (q,k,v,o,gate,up,down), tile-sharded",
+             "c5": "config 5: OLMoE MoE layer (64 experts), whole experts per GPU",
+             "v2": "b=4 (k=2, V=2): one 1024x1024 weight per GPU"}
     result = None
     if rank == 0:
+        if gather:
+            collective = ("NCCL all_gather_into_tensor per weight on a side stream, each behind "
+                          "its weight's forward launch (overlapped with the next weights' "
+                          "kernels and the backward)")
+        else:
+            collective = "none"
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak" if weak else "strong",
+            "higher_is_better": True, "scaling": "weak" if args.config in ("c2", "v2") else "strong",
             "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded randn codebook and weights, BASELINE configs)",
-            "config": {"workload": {"c2": "config 2: one 1024x1024 weight per GPU",
-                                    "c3": "config 3: Llama-3.2-1B layer, sharded",
-                                    "c5": "config 5: OLMoE MoE layer, sharded",
-                                    "v2": "b=4 (k=2, V=2): one 1024x1024 weight per GPU"}[args.config]
+            "data": "synthetic (seeded randn codebook and weights of the workload's shapes)",
+            "config": {"workload": names[args.config]
                        + f" (L=16, k=2, V={V}, N={NSTEP}, T={args.temperature:g}, {args.weights} weights,"
                          " fwd+bwd, grad=ones)",
-                       "sequences_per_gpu": Bl, "sequences_total": Bl * world if (weak or args.sequences) else total_seqs,
-                       "l2": "flushed between timed steps (256 MB write, outside the events)",
-                       "collective": "NCCL all_gather of soft per step" if world > 1 else "none"},
+                       "sequences_per_gpu": Bl, "sequences_total": total_seqs,
+                       "l2": "flushed between timed steps (256 MB write, outside the events); "
+                             "inputs larger than L2",
+                       "collective": collective},
             "clocks": clk,
             "gpu_launches": launches_per_step * args.steps,
             "kernel_ms": {"forward": fwd_avg, "backward": bwd_avg},
             "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "Gop/s", "frac": achieved / peak,
-                         "traffic": DRAM_BYTES_PER_SEQ[V][dom] * Bl if DRAM_BYTES_PER_SEQ[V] else None,
-                         "traffic_unit": "bytes per launch (ncu capture of 296 / 297 sequences "
+                         "traffic": DRAM_BYTES_PER_SEQ[V][dom] * Bl,
+                         "traffic_unit": "bytes per launch (ncu capture of a small launch "
                                          "scaled by sequences; see profiles/)",
                          "note": f"algorithmic MUFU ops: {MUFU_FWD}/{MUFU_BWD} per state-step "
-                                 f"(fwd/bwd call), peak = {sms} SMs x 16/clk x {clk_mhz:.0f} MHz"},
-            "e2e": {"value": e2e_value, "unit": UNIT,
+                                 f"(fwd/bwd call), peak = {sms} SMs x 16/clk x {clk_mhz:.0f} MHz "
+                                 "(derived; not in MEASURED_PEAKS.json)"},
+            "fp32_issue": fp32,
+            "e2e": {"value": e2e_value, "unit": UNIT, "steps": e2e_steps,
                     "h2d_bytes_per_step": w_host.numel() * 4,
-                    "d2h_bytes_per_step": (soft_host.numel() + dseq_host.numel()) * 4},
+                    "d2h_bytes_per_step": (soft_host.numel() + dseq_host.numel()) * 4,
+                    "api": "quant_2bit_b200.distributed.sharded_bcjr_layer (autograd)"},
         }
+        if gather:
+            result["gather"] = {"exposed_ms_per_step": sum(tail_ms) / len(tail_ms),
+                                "step_ms_without_gathers": t_nogather,
+                                "cost_share": 1.0 - t_nogather / (t_max_ms / args.steps),
+                                "bytes_received_per_rank": sum(
+                                    c - (hi - lo) for c, (lo, hi) in zip(shards.counts, shards.ranges))
+                                * NSTEP * V * 4}
         if world > 1:
-            result["e2e"]["note"] = "per rank: H2D of its shard, D2H of its soft and d_seq"
+            result["e2e"]["note"] = "per rank: H2D of its shard, D2H of its soft rows and d_seq"
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if float(nbad.item()) != 0.0:
+        print("bench: non-finite outputs after the timed region (a device-side wait gave up or "
+              "the inputs are not finite); no number reported", file=sys.stderr, flush=True)
+        raise SystemExit(1)
     if rank == 0:
         if not args.no_cpu_baseline and world == 1:
-            result["cpu_baseline"] = cpu_reference(args, rank)
+            result["cpu_baseline"] = cpu_reference(args, args.cpu_sample_seqs, 1, 1)
         print(json.dumps(result), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c3", choices=["c2", "c3", "c5", "v2", "layer", "viterbi"])
+    ap.add_argument("--temperature", type=float, default=TEMP,
+                    help="T (config 4 sweeps 4, 2, 1, 0.5, 0.25, 0.1, 0.05)")
+    ap.add_argument("--weights", default="gauss", choices=["gauss", "t3"],
+                    help="config 4's Student-t(3) weights with --config c2")
+    ap.add_argument("--cpu-sample-seqs", type=int, default=8,
+                    help="sequences of the CPU baseline leg (one reference chunk)")
+    ap.add_argument("--ref-sample-seqs", type=int, default=2,
+                    help="sequences per step of --impl reference")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sequences", type=int, default=0,
+                    help="use only this many sequences per GPU (small cases for ncu)")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+
+    V, NSTEP = SHAPES[args.config]
+    EDGES_PER_SEQ = NSTEP * (1 << L) * (1 << (K_BITS * V))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        nsample = args.ref_sample_seqs
+        ref = cpu_reference(args, nsample, args.steps, args.warmup)
+        nsample = ref.get("sample_sequences", nsample)
+        line = {"metric": VITERBI_METRIC if args.config == "viterbi" else METRIC,
+                "value": ref["value"], "unit": UNIT, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": nsample * EDGES_PER_SEQ / ref["value"] * 1e3,
+                "higher_is_better": True,
+                "scaling": "weak" if args.config in ("c2", "v2", "viterbi") else "strong",
+                "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic (seeded randn codebook and weights of the workload's shapes)",
+                "impl": "reference",
+                "config": {"workload": f"{args.config}: L=16 k=2 V={V} N={NSTEP} T={args.temperature:g} "
+                                       f"{args.weights} weights, CPU sample of {nsample} sequence(s) per step",
+                           "sample_sequences": nsample},
+                "cpu_baseline": ref,
+                "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    if args.config == "layer":
+        run_layer(args, rank, world, local_rank)
+    elif args.config == "viterbi":
+        run_viterbi(args, rank, world, local_rank)
+    else:
+        run_bcjr(args, rank, world, local_rank)
 
 
 if __name__ == "__main__":

@@ -14,6 +14,14 @@
  * buffer, including the workspace, whose size comes from
  * bcjr_workspace_bytes().  Calls on the same workspace must not overlap.
  *
+ * Failures on the device are never silent: when a bounded device-side wait
+ * gives up (BCJR_ERR_TIMEOUT in the workspace status word, read by
+ * bcjr_ws_status), every output written after the failure was recorded --
+ * always including those of the sequences whose wait expired -- is NaN, and
+ * so is every output of a call whose device temperature T is not positive
+ * and finite.  NaN and infinite inputs propagate to the outputs of their
+ * sequences, as in the reference.
+ *
  * Reference interfaces replaced (Venugopalan2610/quant-2bit):
  *   src/bcjr/bcjr_monolithic.py:157-243  BcjrForwardBackwardMonolithic
  *   src/bcjr/forward_backward.py:190-232  bcjr_forward_backward
@@ -62,6 +70,24 @@ enum {
 
 /* Library version (major * 10000 + minor * 100 + patch). */
 BCJR_API int bcjr_version(void);
+
+/* Test and diagnostic switches, process-wide, all 0 by default.  Nothing in
+ * the library reads the environment.  No counterpart in the reference.
+ *   BCJR_OPT_TEST_DROP_SENDS      1: CTA 1 of every cluster kernel withholds
+ *                                 its messages, so bounded waits expire
+ *                                 (tests of the timeout path only)
+ *   BCJR_OPT_FORCE_GENERIC        1: one-block-per-sequence kernels for all
+ *                                 shapes (cross-checks of the cluster kernels)
+ *   BCJR_OPT_L16_FORWARD_CLUSTER  2 or 4: cluster size of the L=16, k=2, V=1
+ *   BCJR_OPT_L16_BACKWARD_CLUSTER   forward / backward (0: automatic)
+ * Returns the previous value, or -1 for an unknown option. */
+enum {
+    BCJR_OPT_TEST_DROP_SENDS = 1,
+    BCJR_OPT_FORCE_GENERIC = 2,
+    BCJR_OPT_L16_FORWARD_CLUSTER = 3,
+    BCJR_OPT_L16_BACKWARD_CLUSTER = 4
+};
+BCJR_API int bcjr_set_test_option(int option, int value);
 
 /* Static string for a status code. */
 BCJR_API const char *bcjr_status_string(int status);
@@ -138,14 +164,19 @@ BCJR_API int bcjr_ws_status(const void *ws, bcjr_stream_t stream);
  * bcjr_fb_forward.
  *
  * Scratch is a fixed 64 MiB array inside this library's device image, held
- * by every GPU that loads the library until the process exits.  A shape
- * whose single sequence slot does not fit (L=16, k=2, V=1: N above ~980) is
- * rejected with BCJR_ERR_WORKSPACE; smaller shapes run on as many slots as
- * fit, which is slower than bcjr_fb_forward for large batches.  The first
- * call on each device looks up the array's device address
- * (cudaGetSymbolAddress); make it before any stream capture.  All calls
- * share the array: calls that overlap on the GPU race and must be
- * serialised by the caller.  Allocates nothing, on the host or the device.
+ * by every GPU that loads the library until the process exits.  One
+ * sequence slot takes (N + 3) 2^(L - kV) + 2N floats (+1 when that is odd);
+ * a shape whose single slot does not fit is rejected with
+ * BCJR_ERR_WORKSPACE (at L=16, k=2, V=1: N > 1020).  Smaller shapes run on
+ * as many slots as fit, one block per slot, each block taking the next
+ * sequence when it finishes one; that is slower than bcjr_fb_forward for
+ * large batches.  The first call on each device (and the first after the
+ * device's context was reset and re-created) looks up the array's device
+ * address with cudaGetSymbolAddress; make it before any stream capture.
+ * All calls share the array and it keeps the last call's contents (the
+ * kernel writes every element before reading it): calls that overlap on the
+ * GPU race and must be serialised by the caller.  Allocates nothing, on the
+ * host or the device.
  */
 BCJR_API int bcjr_fb_forward_noalloc(const float *seq, const float *cb, const float *T_dev,
                                      int B, int N, int L, int k, int V,

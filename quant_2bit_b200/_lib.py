@@ -4,6 +4,7 @@ The product path has no fallback: if the library is missing or fails to
 load, every op raises.  Pointers handed to the library come from torch CUDA
 tensors; the stream is the caller's current torch stream.
 """
+import contextlib
 import ctypes
 import os
 
@@ -22,6 +23,11 @@ BCJR_ERR_LAUNCH = 6
 BCJR_ERR_DEVICE = 7
 BCJR_ERR_TIMEOUT = 8
 WS_FORWARD, WS_BACKWARD, WS_INTERNALS = 1, 2, 4
+# bcjr_set_test_option switches (tests and diagnostics only)
+OPT_TEST_DROP_SENDS = 1
+OPT_FORCE_GENERIC = 2
+OPT_L16_FORWARD_CLUSTER = 3
+OPT_L16_BACKWARD_CLUSTER = 4
 
 # Every symbol include/bcjr_b200.h declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -29,6 +35,7 @@ _I = ctypes.c_int
 _SZ = ctypes.c_size_t
 SIGNATURES = {
     "bcjr_version": ([], _I),
+    "bcjr_set_test_option": ([_I, _I], _I),
     "bcjr_status_string": ([_I], ctypes.c_char_p),
     "bcjr_workspace_bytes": ([_I, _I, _I, _I, _I, _I], _SZ),
     "bcjr_check_shape": ([_I, _I, _I, _I, _I], _I),
@@ -89,6 +96,20 @@ def check(status, what):
     if status == BCJR_ERR_UNSUPPORTED:
         raise ValueError(f"{what}: {status_string(status)}")
     raise BcjrError(status, what)
+
+
+@contextlib.contextmanager
+def test_option(option, value):
+    """Set a bcjr_set_test_option switch for the duration of a block (tests
+    and diagnostics; the library reads no environment)."""
+    lib = load()
+    old = lib.bcjr_set_test_option(option, int(value))
+    if old < 0:
+        raise ValueError(f"unknown test option {option}")
+    try:
+        yield
+    finally:
+        lib.bcjr_set_test_option(option, old)
 
 
 def ptr(t):

@@ -49,13 +49,21 @@ def _require_cuda(t, name):
 
 def _temperature(T_temp, device):
     """Device fp32 scalar for T (the kernels read T on the device; a python
-    float becomes a 0-d tensor as in forward_backward.py:212-213)."""
+    float becomes a 0-d tensor as in forward_backward.py:212-213).
+
+    A python number must be positive and finite (ValueError otherwise; the
+    reference divides by it unchecked, forward_backward.py:101).  A tensor T
+    is not read on the host (that would synchronise): the kernels write NaN
+    into every output when the T they read is not positive."""
     if torch.is_tensor(T_temp):
         T = T_temp.detach()
         if T.device != device or T.dtype != torch.float32:
             T = T.to(device=device, dtype=torch.float32)
         return T.reshape(()).contiguous()
-    return torch.tensor(float(T_temp), dtype=torch.float32, device=device)
+    Tf = float(T_temp)
+    if not (Tf > 0.0 and math.isfinite(Tf)):
+        raise ValueError(f"temperature must be positive and finite, got {T_temp!r}")
+    return torch.tensor(Tf, dtype=torch.float32, device=device)
 
 
 def _infer_L_k_V(sequences, codebook, preds, k):
@@ -74,10 +82,15 @@ def _infer_L_k_V(sequences, codebook, preds, k):
     return L, k, V
 
 
-def _forward(seq, cb, T, L, k, V, want_logZ=True):
+def _forward(seq, cb, T, L, k, V, want_logZ=True, out=None):
     B, N, _ = seq.shape
     dev = seq.device
-    soft = torch.empty((B, N, V), dtype=torch.float32, device=dev)
+    if out is None:
+        soft = torch.empty((B, N, V), dtype=torch.float32, device=dev)
+    else:
+        assert out.shape == (B, N, V) and out.dtype == torch.float32 and out.is_contiguous() \
+            and out.device == dev, "out must be a contiguous float32 (B, N, V) tensor on the input's device"
+        soft = out
     logZ = torch.empty((B,), dtype=torch.float32, device=dev) if want_logZ else None
     if B == 0:
         return soft, logZ
@@ -173,6 +186,9 @@ class _BcjrSoftLogZ(torch.autograd.Function):
         soft, logZ = _forward(seq, cb, T, L, k, V, want_logZ=True)
         ctx.save_for_backward(seq, cb, T, soft)
         ctx.dims = (L, k, V)
+        # an output that the loss does not use gets None, not a zero tensor
+        # (no eager kernels for an unused log Z)
+        ctx.set_materialize_grads(False)
         return soft, logZ
 
     @staticmethod
@@ -240,10 +256,12 @@ class _MonolithicKV(torch.autograd.Function):
         return d_seq, None, None, None, None, None
 
 
-def bcjr_soft_forward(sequences, codebook, T_temp, L, k, V):
-    """Forward only, no autograd: (soft, log_Z) for inference-style callers."""
+def bcjr_soft_forward(sequences, codebook, T_temp, L, k, V, out=None, want_logZ=True):
+    """Forward only, no autograd: (soft, log_Z) for inference-style callers.
+    ``out``: a contiguous (B, N, V) float32 tensor to write soft into (for
+    instance rows of a larger buffer); log_Z is None unless ``want_logZ``."""
     seq, cb, T = _prep(sequences.float(), codebook.float(), T_temp)
-    return _forward(seq, cb, T, L, k, V, want_logZ=True)
+    return _forward(seq, cb, T, L, k, V, want_logZ=want_logZ, out=out)
 
 
 def bcjr_soft_backward(sequences, codebook, T_temp, soft, grad_soft, L, k, V):

@@ -52,7 +52,8 @@
 //
 // Every wait is bounded (about 1 s); on timeout the kernel records
 // BCJR_ERR_TIMEOUT in the workspace status word, stops waiting and sending,
-// and runs to completion.  The recursions are documented in bcjr_common.cuh.
+// runs to completion, and writes NaN into the outputs it writes from then on
+// (poison_value).  The recursions are documented in bcjr_common.cuh.
 #include <cstdint>
 
 #include "bcjr_cluster.cuh"
@@ -177,6 +178,7 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     const float ikap = T / kLog2e;
     const float two_over_T = 2.f / T;
     const float a0 = -(float)kB * ikap;     // cost of A_0 = b everywhere
+    const bool bad_T = bad_temperature(T);  // outputs NaN (poison_value)
 
     // Each thread carries kVT work units; unit h of thread (warp, lane) is
     // virtual warp vw = warp + kWarps h, lane `lane` of a 512-unit layout.
@@ -487,7 +489,7 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             for (int r = 0; r < kCL; ++r) smin_merge(m, s, sm.lz[z][r][0], sm.lz[z][r][1]);
             logZ2[z] = -((double)kap * O[z] + (double)m - (double)log2f(s));
             if (!GRAD && rank == 0 && tid == 0 && logZ_out)
-                logZ_out[sidx[z]] = (float)(logZ2[z] * (double)kLn2);
+                logZ_out[sidx[z]] = (float)(logZ2[z] * (double)kLn2) + poison_value(bad_T, status);
         }
         if (tid == 0) {
 #pragma unroll
@@ -640,6 +642,7 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         cluster_sync();
         if (rank == 0) {
             const float scale = GRAD ? two_over_T : 1.f;
+            const float poison = poison_value(bad_T, status);   // NaN after a failed wait
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
@@ -653,8 +656,8 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                         s0 += v.x + v.z;
                         s1 += v.y + v.w;
                     }
-                    out[(sidx[z] * N + tn) * kV] = scale * s0;
-                    out[(sidx[z] * N + tn) * kV + 1] = scale * s1;
+                    out[(sidx[z] * N + tn) * kV] = scale * s0 + poison;
+                    out[(sidx[z] * N + tn) * kV + 1] = scale * s1 + poison;
                 }
             }
         }

@@ -3,13 +3,25 @@
 // Validates shapes and pointers, sizes the persistent grid from the caller's
 // workspace, and launches the kernels on the caller's stream.  No host
 // synchronisation, no allocation, T is read on the device.
+#include <atomic>
 #include <cstdint>
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "../../include/bcjr_b200.h"
 #include "bcjr_kernels.h"
+
+namespace bcjr {
+
+namespace {
+std::atomic<int> g_test_options[kOptCount];
+}  // namespace
+
+int test_option(int which) {
+    return (which > 0 && which < kOptCount) ? g_test_options[which].load(std::memory_order_relaxed) : 0;
+}
+
+}  // namespace bcjr
 
 namespace {
 
@@ -64,11 +76,10 @@ bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 // and V=2 (bcjr_b4.cu), forward and backward, for 2 <= N <= 512; they read
 // the codebook with 16-byte vector loads, so a codebook pointer that is not
 // 16-byte aligned (a view at an odd offset) takes the generic kernels, as do
-// every other shape, the internals, and BCJR_B200_FORCE_GENERIC=1.
+// every other shape, the internals, and the BCJR_OPT_FORCE_GENERIC option.
 int pick_kernel(int B, int N, int L, int b, int V, int mode, const void *cb) {
     if (mode == bcjr::kModeInternals) return bcjr::kKernelGeneric;
-    const char *env = std::getenv("BCJR_B200_FORCE_GENERIC");
-    if (env && env[0] == '1') return bcjr::kKernelGeneric;
+    if (bcjr::test_option(bcjr::kOptForceGeneric)) return bcjr::kKernelGeneric;
     if (cb && !aligned(cb, 16)) return bcjr::kKernelGeneric;
     if (bcjr::l16_applicable(B, N, L, b, V) && bcjr::l16_clusters(B, mode) > 0)
         return bcjr::kKernelL16;
@@ -113,10 +124,9 @@ int prepare(bcjr::LaunchArgs &a, void *ws, size_t ws_bytes, int mode) {
     a.ws_data = static_cast<char *>(ws) + kHeaderBytes;
     a.ws_data_bytes = ws_bytes - kHeaderBytes;
     a.mode = mode;
-    // Test-only: BCJR_B200_TEST_DROP_SENDS=1 makes the cluster kernel's CTA 1
-    // withhold its outputs so that the bounded waits time out (tests/ only).
-    const char *drop = std::getenv("BCJR_B200_TEST_DROP_SENDS");
-    a.drop_sends = (drop && drop[0] == '1') ? 1 : 0;
+    // Test-only (BCJR_OPT_TEST_DROP_SENDS): the cluster kernel's CTA 1
+    // withholds its outputs so that the bounded waits time out.
+    a.drop_sends = bcjr::test_option(bcjr::kOptDropSends) ? 1 : 0;
     a.grid = a.kernel != bcjr::kKernelGeneric ? 1 : bcjr::generic_grid(a.B, a.N, a.L, a.BB, mode, a.ws_data_bytes);
     if (a.grid < 1) return BCJR_ERR_WORKSPACE;
     if (cudaMemsetAsync(a.status, 0, sizeof(int) + sizeof(unsigned), a.stream) != cudaSuccess)
@@ -140,7 +150,12 @@ cudaError_t launch(const bcjr::LaunchArgs &a) {
 
 extern "C" {
 
-int bcjr_version(void) { return 100; }
+int bcjr_version(void) { return 200; }
+
+int bcjr_set_test_option(int option, int value) {
+    if (option <= 0 || option >= bcjr::kOptCount) return -1;
+    return bcjr::g_test_options[option].exchange(value);
+}
 
 const char *bcjr_status_string(int status) {
     switch (status) {

@@ -64,6 +64,19 @@ __device__ __forceinline__ float rcp(float x) {
     return y;
 }
 
+// Failure policy.  A call whose temperature is not positive and finite, or
+// in which a bounded device-side wait gave up (non-zero status word), must
+// not return numbers that look valid: every output gets poison_value() added,
+// NaN in those cases and 0 otherwise, so the failure reaches the caller
+// without a host synchronisation.
+__device__ __forceinline__ bool bad_temperature(float T) {
+    return !(T > 0.f && T < __builtin_huge_valf());
+}
+__device__ __forceinline__ float poison_value(bool bad, const int *status) {
+    if (!bad && status) bad = *reinterpret_cast<const volatile int *>(status) != 0;
+    return bad ? __int_as_float(0x7fffffff) : 0.f;
+}
+
 // Sum of NV values over a thread block; every thread gets the result.
 // `sh` must hold (blockDim.x / 32) * NV floats plus NV.  Contains two
 // __syncthreads().

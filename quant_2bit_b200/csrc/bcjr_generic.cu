@@ -193,6 +193,7 @@ gen_forward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     const int G = 1 << (L - BB);
     const float T = __ldg(T_dev);
     const float kappa = kLog2e / T;
+    const float poison = poison_value(bad_temperature(T), nullptr);   // NaN for an unusable T
     const Slot sl = make_slot(ws + (long)blockIdx.x * slot_floats, N, L, BB, mode);
     const bool internals = (mode == kModeInternals);
 
@@ -201,7 +202,7 @@ gen_forward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         alpha_sweep<BB, V, false>(w, cb, nullptr, nullptr, N, L, kappa, sl.Ah, nullptr,
                                   sl.Off, smax);
         const double logZ2 = log2_partition(sl.Ah + (long)N * G, G, sl.Off, N, sh);
-        if (threadIdx.x == 0 && logZ) logZ[bs] = (float)(logZ2 * (double)kLn2);
+        if (threadIdx.x == 0 && logZ) logZ[bs] = (float)(logZ2 * (double)kLn2) + poison;
 
         // beta sweep (backward in time) with P and soft for step t+1
         float *Rlast = internals ? sl.Bt + (long)(N - 1) * G : sl.Bt + (long)((N - 1) & 1) * G;
@@ -271,7 +272,7 @@ gen_forward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 block_sum<V>(accf, sh);
                 if (threadIdx.x == 0) {
 #pragma unroll
-                    for (int v = 0; v < V; ++v) soft[((long)bs * N + tn) * V + v] = accf[v];
+                    for (int v = 0; v < V; ++v) soft[((long)bs * N + tn) * V + v] = accf[v] + poison;
                 }
             }
         }
@@ -291,9 +292,9 @@ gen_forward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                 for (long s = threadIdx.x; s < S; s += blockDim.x) {
                     const float a2 = energy2<V>(cb, s, wt, kappa) + St[s >> BB];
                     const float b2 = Rt[s & (G - 1)];
-                    if (LAout) LAout[base + s] = (float)(((double)a2 + Oa) * (double)kLn2);
-                    if (LBout) LBout[base + s] = (float)(((double)b2 + Ub) * (double)kLn2);
-                    if (Pout) Pout[base + s] = exp2f(a2 + b2 - Cp);
+                    if (LAout) LAout[base + s] = (float)(((double)a2 + Oa) * (double)kLn2) + poison;
+                    if (LBout) LBout[base + s] = (float)(((double)b2 + Ub) * (double)kLn2) + poison;
+                    if (Pout) Pout[base + s] = exp2f(a2 + b2 - Cp) + poison;
                 }
             }
             __syncthreads();
@@ -314,6 +315,7 @@ gen_backward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     const int G = 1 << (L - BB);
     const float T = __ldg(T_dev);
     const float kappa = kLog2e / T;
+    const float poison = poison_value(bad_temperature(T), nullptr);   // NaN for an unusable T
     const float two_over_T = 2.f / T;
     const Slot sl = make_slot(ws + (long)blockIdx.x * slot_floats, N, L, BB, kModeBackward);
 
@@ -405,7 +407,7 @@ gen_backward_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             block_sum<V>(accf, sh);
             if (threadIdx.x == 0) {
 #pragma unroll
-                for (int v = 0; v < V; ++v) dseq[((long)bs * N + tn) * V + v] = two_over_T * accf[v];
+                for (int v = 0; v < V; ++v) dseq[((long)bs * N + tn) * V + v] = two_over_T * accf[v] + poison;
             }
         }
         __syncthreads();

@@ -7,6 +7,17 @@
 namespace bcjr {
 
 enum { kModeForward = 0, kModeBackward = 1, kModeInternals = 2 };
+
+// Test and diagnostic switches, set through bcjr_set_test_option() (C ABI);
+// all zero unless a test sets them (nothing reads the environment).
+enum {
+    kOptDropSends = 1,       // BCJR_OPT_TEST_DROP_SENDS
+    kOptForceGeneric = 2,    // BCJR_OPT_FORCE_GENERIC
+    kOptL16Forward = 3,      // BCJR_OPT_L16_FORWARD_CLUSTER
+    kOptL16Backward = 4,     // BCJR_OPT_L16_BACKWARD_CLUSTER
+    kOptCount = 5
+};
+int test_option(int which);   // bcjr_capi.cu
 enum { kKernelGeneric = 0, kKernelL16 = 1, kKernelB4 = 2 };
 
 struct LaunchArgs {

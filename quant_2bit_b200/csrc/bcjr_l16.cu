@@ -56,9 +56,9 @@
 //
 // Every wait is bounded (about 1 s); on timeout the kernel records
 // BCJR_ERR_TIMEOUT in the workspace status word, stops waiting and sending,
-// and runs to completion.  The recursions are documented in bcjr_common.cuh.
+// runs to completion, and writes NaN into the outputs it writes from then on
+// (poison_value).  The recursions are documented in bcjr_common.cuh.
 #include <cstdint>
-#include <cstdlib>
 
 #include "bcjr_cluster.cuh"
 #include "bcjr_kernels.h"
@@ -196,6 +196,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     const float ikap = T / kLog2e;
     const float two_over_T = 2.f / T;
     const float a0 = -(float)kB * ikap;     // cost of A_0 = b everywhere
+    const bool bad_T = bad_temperature(T);  // outputs NaN (poison_value)
 
     // Codebook of my kJPT butterflies:
     // cq[jj][c][h] = (c(2h, c), c(2h+1, c)),  c(p, c) = cb[p 2^14 + 4 j + c].
@@ -311,17 +312,37 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 
     // Sequences are claimed kSlots at a time from a counter shared by every
     // cluster of the call (of both instances, when two run side by side):
-    // CTA 0 takes the claim and publishes it to the cluster.
-    auto claim_next = [&]() -> long {
+    // CTA 0 takes the claim and publishes it to the cluster, with the top bit
+    // set once the call has failed (a bounded wait gave up anywhere).  A
+    // failed call keeps claiming, but its clusters only write NaN into the
+    // claimed sequences' outputs: no output of a failed call is left
+    // unwritten or looks valid.
+    auto claim_next = [&]() -> unsigned {
         if (rank == 0 && tid == 0) {
-            const unsigned s0 = failed ? 0x7fffffffu : atomicAdd(claim, (unsigned)kSlots);
+            unsigned s0 = atomicAdd(claim, (unsigned)kSlots);
+            if (*reinterpret_cast<volatile int *>(status) != 0) s0 |= 0x80000000u;
 #pragma unroll
             for (int r = 0; r < kCL; ++r) st_cluster_u32(cbase[r] + soff(&sm.next), s0);
         }
         cluster_sync();
-        return (long)sm.next;
+        return sm.next;
     };
-    for (long first = claim_next(); first < B; first = claim_next()) {
+    for (unsigned cl = claim_next(); (long)(cl & 0x7fffffffu) < B; cl = claim_next()) {
+        const long first = (long)(cl & 0x7fffffffu);
+        if (cl >> 31) {
+            if (rank == 0) {
+                const float nanv = __int_as_float(0x7fffffff);
+#pragma unroll
+                for (int z = 0; z < kSlots; ++z) {
+                    const long sz = first + z;
+                    if (sz >= B) continue;
+                    for (int t = tid; t < N; t += kNT) out[sz * N + t] = nanv;
+                    if (!GRAD && tid == 0 && logZ_out) logZ_out[sz] = nanv;
+                }
+            }
+            cluster_sync();   // every thread has read this claim before the next one is published
+            continue;
+        }
         bool active[kSlots];
         long sidx[kSlots];
         float *slot_ws[kSlots];
@@ -470,7 +491,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
             for (int i = 0; i < kParts; ++i) smin_merge(m, s, sm.lz[z][i][0], sm.lz[z][i][1]);
             logZ2[z] = -((double)kap * O[z] + (double)m - (double)log2f(s));
             if (!GRAD && rank == 0 && tid == 0 && logZ_out)
-                logZ_out[sidx[z]] = (float)(logZ2[z] * (double)kLn2);
+                logZ_out[sidx[z]] = (float)(logZ2[z] * (double)kLn2) + poison_value(bad_T, status);
         }
         if (tid == 0) {
             asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -628,6 +649,9 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
         cluster_sync();
         if (rank == 0) {
             const float scale = GRAD ? two_over_T : 1.f;
+            // NaN if a wait of this cluster (or any earlier failure of the
+            // call) gave up: the cluster_sync above orders its status write
+            const float poison = poison_value(bad_T, status);
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
@@ -640,7 +664,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                         const float4 v = __ldcg(p4 + i);
                         sum += ((v.x + v.y) + v.z) + v.w;
                     }
-                    out[sidx[z] * N + tn] = scale * sum;
+                    out[sidx[z] * N + tn] = scale * sum + poison;
                 }
             }
         }
@@ -753,9 +777,10 @@ cudaError_t launch(const LaunchArgs &a, int ncl, float *ws, bool dependent) {
 // 2-CTA grid on the SMs it leaves free, launched as its programmatic
 // dependent; both take sequences from one counter (measured on B200 with
 // 4096 sequences: 2-CTA alone 114 ms, 4-CTA alone 116 ms, both ~105 ms).
-// BCJR_B200_L16_BACKWARD=2 or =4 runs one instance alone in the backward,
-// BCJR_B200_L16_FORWARD=4 the 4-CTA instance in the forward (tests).  Results
-// do not depend on the instance that runs a sequence.
+// The BCJR_OPT_L16_BACKWARD_CLUSTER option (2 or 4) runs one instance alone
+// in the backward, BCJR_OPT_L16_FORWARD_CLUSTER=4 the 4-CTA instance in the
+// forward (tests).  Results do not depend on the instance that runs a
+// sequence.
 
 namespace {
 
@@ -768,8 +793,7 @@ Plan plan_for(int B, int mode) {
     Plan p;
     const long b = B > 0 ? B : 1;
     const bool bwd = mode == kModeBackward;
-    const char *env = std::getenv(bwd ? "BCJR_B200_L16_BACKWARD" : "BCJR_B200_L16_FORWARD");
-    const int force = env ? std::atoi(env) : 0;
+    const int force = test_option(bwd ? kOptL16Backward : kOptL16Forward);
     const int max2 = l16::max_clusters(mode);
     const long need2 = (b + l16::slots(mode) - 1) / l16::slots(mode);
     const int max4 = l16c4::max_clusters(mode);

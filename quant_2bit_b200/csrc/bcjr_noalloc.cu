@@ -9,19 +9,25 @@
 // of a caller-provided workspace.
 //
 // The scratch is kNoAllocScratchBytes (64 MiB).  Every GPU that loads the
-// library holds it until the process exits.  A call whose single sequence
-// slot does not fit (for L=16, k=2, V=1 that is N > ~980) is rejected with
-// BCJR_ERR_WORKSPACE before anything is launched; otherwise the batch runs on
-// as many slots as fit.
+// library holds it until the process exits.  One sequence slot of the
+// generic forward takes (N + 3) 2^(L - kV) + 2N floats (+1 when odd); a call
+// whose single slot does not fit (for L=16, k=2, V=1 that is N > 1020) is
+// rejected with BCJR_ERR_WORKSPACE before anything is launched; otherwise
+// the batch runs on as many slots as fit, a block taking the next sequence
+// when it finishes one.
 //
 // Host code must not use `g_scratch` itself: in host code that name is only a
 // host-side stand-in, not a device address.  The first call on each device
 // (with that device current) looks up the array's device address with
-// cudaGetSymbolAddress and caches it; make that first call before any stream
-// capture.  All calls share the one array, so calls whose work overlaps on
-// the GPU (different streams, or different host threads) race on it and must
-// be serialised by the caller.  Nothing in the array needs to start at zero:
-// the kernel writes every element it reads before reading it.
+// cudaGetSymbolAddress and caches it together with the identity of the
+// device's current context; a call that finds another context (the device
+// was reset and its context re-created, which reloads the module) looks the
+// address up again.  Make the first call before any stream capture.  All
+// calls share the one array, so calls whose work overlaps on the GPU
+// (different streams, or different host threads) race on it and must be
+// serialised by the caller.  The array keeps the last call's contents;
+// nothing in it needs to start at zero: the kernel writes every element it
+// reads before reading it.
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -35,19 +41,55 @@ constexpr size_t kNoAllocScratchBytes = 64ull << 20;
 
 static __device__ __align__(256) unsigned char g_scratch[kNoAllocScratchBytes];
 
-// Device address of g_scratch on `dev` (looked up once per device).
+// Unique id of the calling thread's current CUDA context (cuCtxGetId), 0
+// when there is none or it cannot be had.  The driver functions come through
+// the runtime's entry-point query, so the library needs no link against the
+// driver library.
+unsigned long long current_context_id() {
+    using GetCurrent = int (*)(void **);
+    using GetId = int (*)(void *, unsigned long long *);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        p = nullptr;
+        q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+        cudaGetLastError();
+    });
+    if (!get_current || !get_id) return 0;
+    void *ctx = nullptr;
+    if (get_current(&ctx) != 0 || !ctx) return 0;
+    unsigned long long id = 0;
+    return get_id(ctx, &id) == 0 ? id : 0;
+}
+
+// Device address of g_scratch on `dev` (the current device): looked up once
+// per device and context.  Without a context id (none current yet, or the
+// query unavailable) it is looked up on every call.
 int scratch_address(int dev, void **out) {
     static std::mutex mu;
     static void *addr[64] = {};
+    static unsigned long long ctx_of[64] = {};
     if (dev < 0 || dev >= 64) return BCJR_ERR_DEVICE;
     std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev]) {
+    const unsigned long long ctx = current_context_id();
+    if (!addr[dev] || ctx == 0 || ctx != ctx_of[dev]) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || !p) {
             cudaGetLastError();
+            addr[dev] = nullptr;
             return BCJR_ERR_DEVICE;
         }
         addr[dev] = p;
+        ctx_of[dev] = current_context_id();   // the lookup made the context current
     }
     *out = addr[dev];
     return BCJR_OK;

@@ -257,9 +257,15 @@ __global__ void vit_b4_backtrace(const unsigned char *__restrict__ bp_all,
                                  const int *__restrict__ final_states,
                                  const float *__restrict__ seq, const float *__restrict__ cb, int B,
                                  int N, int *__restrict__ bits, int *__restrict__ starts,
-                                 float *__restrict__ recon, float *__restrict__ mse) {
+                                 float *__restrict__ recon, float *__restrict__ mse,
+                                 const int *__restrict__ status) {
     const long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
+    // After a failed wait the walk is not the optimum: NaN reconstructions
+    // and MSEs (the bitstreams stay in range, see below).  Selected, not
+    // added, so that reconstructions stay bit-exact codebook values.
+    const bool failed = poison_value(false, status) != 0.f;
+    const float nanv = __int_as_float(0x7fffffff);
     // The masks keep every index in range whatever the arrays hold: after a
     // wait timeout (BCJR_ERR_TIMEOUT) the forward kernel leaves backpointers
     // and final states unwritten, and this walk must still read in bounds.
@@ -269,8 +275,8 @@ __global__ void vit_b4_backtrace(const unsigned char *__restrict__ bp_all,
         const long i = b * N + t;
         bits[i] = s & 15;
         const float r0 = __ldg(cb + 2 * (size_t)s), r1 = __ldg(cb + 2 * (size_t)s + 1);
-        recon[2 * i] = r0;
-        recon[2 * i + 1] = r1;
+        recon[2 * i] = failed ? nanv : r0;
+        recon[2 * i + 1] = failed ? nanv : r1;
         const double d0 = (double)r0 - (double)__ldg(seq + 2 * i);
         const double d1 = (double)r1 - (double)__ldg(seq + 2 * i + 1);
         e2 += d0 * d0 + d1 * d1;
@@ -279,7 +285,7 @@ __global__ void vit_b4_backtrace(const unsigned char *__restrict__ bp_all,
         else s = h;   // step 0's backpointers are all 0
     }
     starts[b] = s;
-    mse[b] = (float)(e2 / (2.0 * N));
+    mse[b] = failed ? nanv : (float)(e2 / (2.0 * N));
 }
 
 }  // namespace vb4
@@ -352,7 +358,7 @@ cudaError_t launch_vit_b4(const float *seq, const float *cb, int B, int N, int *
         if (e != cudaSuccess) return e;
         vb4::vit_b4_backtrace<<<(nb + 127) / 128, 128, 0, st>>>(
             bp, finals, seq + b0 * N * 2, cb, nb, N, bits + b0 * N, starts + b0, recon + b0 * N * 2,
-            mse + b0);
+            mse + b0, status);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }

@@ -201,8 +201,7 @@ extern "C" {
 constexpr size_t kVitHeader = 256;
 
 bool vit_use_cluster(int N, int L, int k, int V, const void *cb) {
-    const char *env = std::getenv("BCJR_B200_FORCE_GENERIC");
-    if (env && env[0] == '1') return false;
+    if (bcjr::test_option(bcjr::kOptForceGeneric)) return false;
     return bcjr::vit_b4_applicable(N, L, k, V, cb);
 }
 
@@ -244,12 +243,11 @@ BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L
     const size_t data_bytes = ws_bytes - kVitHeader;
     if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return BCJR_ERR_LAUNCH;
     if (vit_use_cluster(N, L, k, V, cb) && data_bytes >= bcjr::vit_b4_workspace_bytes(B, N)) {
-        // Test-only: BCJR_B200_TEST_DROP_SENDS=1 makes the cluster kernel's CTA 1
-        // withhold its outputs so that the bounded waits time out (tests/ only).
-        const char *drop = std::getenv("BCJR_B200_TEST_DROP_SENDS");
+        // Test-only (BCJR_OPT_TEST_DROP_SENDS): the cluster kernel's CTA 1
+        // withholds its outputs so that the bounded waits time out.
         const cudaError_t e = bcjr::launch_vit_b4(seq, cb, B, N, bitstreams, start_states, recons,
                                                   mses, data, data_bytes, status,
-                                                  (drop && drop[0] == '1') ? 1 : 0, s);
+                                                  bcjr::test_option(bcjr::kOptDropSends) ? 1 : 0, s);
         return e == cudaSuccess ? BCJR_OK : BCJR_ERR_LAUNCH;
     }
     const size_t slot = bcjr::vit::slot_bytes(N, L, k * V);

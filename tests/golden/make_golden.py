@@ -11,7 +11,7 @@ Input generation follows the benchmark configs: torch.Generator seeded with
 ``seed``; the codebook is drawn first, then the weights; Student-t weights use
 numpy.random.default_rng(seed).standard_t(3) / sqrt(3).
 
-    python tests/golden/make_golden.py --ref <reference root> [--only c1|small|l16|v2|v2sweep|rht|viterbi]
+    python tests/golden/make_golden.py --ref <reference root> [--only c1|small|l16|v2|v2sweep|rht|viterbi|c3|c5|dropin]
 """
 import argparse
 import math
@@ -91,6 +91,106 @@ def gen_l16(ref_fb, nseq=2):
             save(f"l16_{dist}_T{T:g}.npz", w=w, grad=grad, T=np.float64(T),
                  L=L, k=k, V=V, **out)
             print(f"  {dist} T={T}: {time.time() - t0:.0f}s", flush=True)
+
+
+def _pick_tiles(scale_rows, m, n, count):
+    """Indices (reference tile order, column block 0) of the `count` tiles
+    whose 16 rows have the largest mean scale."""
+    per_tile = scale_rows.view(m // 16, 16).mean(1)
+    return [int(i) for i in torch.argsort(per_tile, descending=True)[:count]]
+
+
+def gen_layer(ref_fb, config):
+    # Configs 3 and 5 as bench.py builds them (bench.layer_matrix): weights
+    # scaled by U[0.5, 2] per row (config 3) or per expert (config 5), so
+    # |w| reaches ~8 at T = 0.5.  A few tiles with the largest scales, T=0.5,
+    # random upstream gradient; `rows` = their indices among all the layer's
+    # sequences (weights concatenated in order).
+    root = os.path.dirname(os.path.dirname(HERE))
+    sys.path.insert(0, root)
+    import bench
+    L, k, V, N, T = 16, 2, 1, 256, 0.5
+    shapes = bench.layer_shapes(config)
+    counts = [(m // 16) * (n // 16) for m, n in shapes]
+    starts = np.cumsum([0] + counts)
+    picks = []   # (weight index, tile index)
+    if config == "c3":
+        for idx, cnt in ((4, 2), (6, 1)):          # gate (8192 x 2048), down (2048 x 8192)
+            m, n = shapes[idx]
+            _, scale = bench.layer_matrix(config, idx)
+            picks += [(idx, i) for i in _pick_tiles(scale[:, 0], m, n, cnt)]
+    else:
+        scales = [float(bench.layer_matrix(config, 3 * e)[1]) for e in range(64)]
+        e = int(np.argmax(scales))
+        picks = [(3 * e, 0), (3 * e + 2, 5)]       # the largest-scale expert's gate and down
+    w = np.stack([bench.tile(bench.layer_matrix(config, idx)[0])[i].numpy() for idx, i in picks])
+    w = w.reshape(len(picks), N, V).astype(np.float32)
+    rows = np.array([starts[idx] + i for idx, i in picks], np.int64)
+    g = torch.Generator().manual_seed(31 if config == "c3" else 53)
+    cb = torch.randn(1 << L, V, generator=torch.Generator().manual_seed(0)).numpy()
+    assert np.array_equal(cb, np.load(os.path.join(HERE, "l16_cb.npy")))
+    grad = torch.randn(len(picks), N, V, generator=g).numpy()
+    t0 = time.time()
+    out = run_ref(ref_fb, w, cb, T, L, k, V, grad)
+    save(f"{config}_scaled_T0.5.npz", w=w, grad=grad, T=np.float64(T), L=L, k=k, V=V, rows=rows,
+         **out)
+    print(f"  {config}: {len(picks)} sequences, max |w| {np.abs(w).max():.2f}, "
+          f"{time.time() - t0:.0f}s", flush=True)
+
+
+def gen_dropin(ref_root):
+    # The reference's own QuantizedLinear(quant_mode="bcjr") pipeline
+    # (src/qat/quantized_linear.py:204-211 -> src/bcjr/bcjr_quant.py:159-178)
+    # on CPU for a 32x64 weight with a HYB codebook at T = 0.5: the RHT as
+    # torch matmuls with Sylvester-Hadamard matrices (checked here against the
+    # reference's numpy apply_rht / apply_inverse_rht, src/rht/transform.py),
+    # the reference's bcjr_quantize_weight_rotated (eager BCJR, chunks of 8
+    # with checkpointing), a linear forward with bias, and an upstream
+    # gradient; W_q, y and W_latent.grad in fp32 and fp64.
+    from src.rht.transform import apply_rht, apply_inverse_rht, make_sign_vector
+    from src.bcjr.bcjr_quant import bcjr_quantize_weight_rotated
+    from src.bcjr.forward_backward import build_pred_succ_tables
+    from src.codes.ref import decode_hyb_batch
+    m, n, seed, T = 32, 64, 7, 0.5
+    lut = np.random.default_rng(21).standard_normal((512, 2)).astype(np.float32)
+    cb = decode_hyb_batch(np.arange(1 << 16, dtype=np.uint32), lut, Q=9).astype(np.float32)
+    sl = make_sign_vector(m, seed=seed)          # as QuantizedLinear(seed=7) makes them
+    sr = make_sign_vector(n, seed=seed + 1)
+    rng = np.random.default_rng(22)
+    W = (0.05 * rng.standard_normal((m, n))).astype(np.float32)
+    bias = (0.1 * rng.standard_normal(m)).astype(np.float32)
+    x = rng.standard_normal((4, n)).astype(np.float32)
+    gy = rng.standard_normal((4, m)).astype(np.float32)
+
+    def sylvester(k):
+        H = np.ones((1, 1))
+        while H.shape[0] < k:
+            H = np.block([[H, H], [H, -H]])
+        return H
+
+    preds, succs = build_pred_succ_tables(device="cpu")
+    out = {}
+    for tag, dt in (("32", torch.float32), ("64", torch.float64)):
+        Hm, Hn = torch.tensor(sylvester(m), dtype=dt), torch.tensor(sylvester(n), dtype=dt)
+        slt, srt = torch.tensor(sl, dtype=dt), torch.tensor(sr, dtype=dt)
+        scale = math.sqrt(m * n)
+        Wt = torch.tensor(W, dtype=dt, requires_grad=True)
+        W_tilde = (Hm @ (slt[:, None] * Wt * srt[None, :]) @ Hn) / scale
+        assert np.allclose(W_tilde.detach().numpy(), apply_rht(W.astype(np.float64), sl, sr),
+                           rtol=1e-5, atol=1e-6)
+        Wq_tilde = bcjr_quantize_weight_rotated(W_tilde, torch.tensor(cb, dtype=dt), float(T),
+                                                preds, succs)
+        Wq = slt[:, None] * (Hm @ Wq_tilde @ Hn) * srt[None, :] / scale
+        assert np.allclose(Wq.detach().numpy(),
+                           apply_inverse_rht(Wq_tilde.detach().numpy().astype(np.float64), sl, sr),
+                           rtol=1e-5, atol=1e-6)
+        y = torch.tensor(x, dtype=dt) @ Wq.T + torch.tensor(bias, dtype=dt)
+        (y * torch.tensor(gy, dtype=dt)).sum().backward()
+        out["Wq" + tag] = Wq.detach().numpy()
+        out["y" + tag] = y.detach().numpy()
+        out["grad" + tag] = Wt.grad.numpy()
+    save("dropin_qlinear_T0.5.npz", W=W, bias=bias, x=x, gy=gy, lut=lut, sign_l=sl, sign_r=sr,
+         seed=seed, T=np.float64(T), m=m, n=n, **out)
 
 
 def gen_v2(ref_fb):
@@ -192,6 +292,10 @@ def main():
             gen_viterbi(args.ref)
         elif what == "v2sweep":
             gen_v2sweep(ref_fb, args.ref)
+        elif what in ("c3", "c5"):
+            gen_layer(ref_fb, what)
+        elif what == "dropin":
+            gen_dropin(args.ref)
         else:
             {"c1": gen_c1, "small": gen_small, "l16": gen_l16, "v2": gen_v2}[what](ref_fb)
 

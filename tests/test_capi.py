@@ -84,3 +84,22 @@ def test_ops_refuse_cpu_tensors():
     cb = torch.randn(256, 1)
     with pytest.raises(RuntimeError, match="CUDA"):
         bcjr_forward_backward(w, cb, 1.0, L=8, k=2, V=1)
+
+
+def test_test_options_are_set_through_the_abi_not_the_environment(lib):
+    """Fault injection and kernel forcing are process-wide switches set by
+    bcjr_set_test_option (0 by default); the library reads no environment
+    variable on any path (no stray export can change a result)."""
+    from quant_2bit_b200 import _lib
+    for opt in (_lib.OPT_TEST_DROP_SENDS, _lib.OPT_FORCE_GENERIC, _lib.OPT_L16_FORWARD_CLUSTER,
+                _lib.OPT_L16_BACKWARD_CLUSTER):
+        assert lib.bcjr_set_test_option(opt, 0) == 0
+        with _lib.test_option(opt, 1):
+            assert lib.bcjr_set_test_option(opt, 1) == 1
+        assert lib.bcjr_set_test_option(opt, 0) == 0
+    assert lib.bcjr_set_test_option(0, 1) == -1
+    assert lib.bcjr_set_test_option(99, 1) == -1
+    csrc = os.path.join(ROOT, "quant_2bit_b200", "csrc")
+    for name in os.listdir(csrc):
+        text = open(os.path.join(csrc, name)).read()
+        assert "getenv" not in text, name

@@ -5,8 +5,6 @@ shortest and longest N it serves, and N beyond it, which falls back), low
 temperature, a HYB codebook built the way the reference's callers build it,
 a misaligned codebook view (served by the generic kernels), and the bounded
 waits."""
-import os
-
 import numpy as np
 import pytest
 import torch
@@ -19,9 +17,8 @@ pytestmark = pytest.mark.gpu
 
 def _run(w, cb, T, grad, generic=False, V=2, cb_offset=0):
     import quant_2bit_b200 as q
-    old = os.environ.get("BCJR_B200_FORCE_GENERIC")
-    os.environ["BCJR_B200_FORCE_GENERIC"] = "1" if generic else "0"
-    try:
+    from quant_2bit_b200 import _lib
+    with _lib.test_option(_lib.OPT_FORCE_GENERIC, 1 if generic else 0):
         dev = torch.device("cuda")
         wd = torch.tensor(w, device=dev)
         if cb_offset:
@@ -36,11 +33,6 @@ def _run(w, cb, T, grad, generic=False, V=2, cb_offset=0):
         d = q.bcjr_soft_backward(wd, cbd, T, soft, torch.tensor(grad, device=dev), 16, 2, V)
         torch.cuda.synchronize()
         return soft.cpu().numpy(), logZ.cpu().numpy(), d.cpu().numpy()
-    finally:
-        if old is None:
-            del os.environ["BCJR_B200_FORCE_GENERIC"]
-        else:
-            os.environ["BCJR_B200_FORCE_GENERIC"] = old
 
 
 def _inputs(seed, B, N, scale=1.0):
@@ -126,11 +118,11 @@ def test_misaligned_codebook_view_takes_generic_path(cuda_ok, V):
 
 
 def test_b4_bounded_wait_timeout_is_reported_and_context_survives(cuda_ok):
-    """Failure detection without a GPU fault: with BCJR_B200_TEST_DROP_SENDS=1
-    one CTA of each cluster withholds its outputs, every consumer's bounded
-    wait (~1 s) expires, the kernel records BCJR_ERR_TIMEOUT in the workspace
-    status word and finishes; the next normal call on the same context is
-    correct."""
+    """Failure detection without a GPU fault: with the test option
+    BCJR_OPT_TEST_DROP_SENDS one CTA of each cluster withholds its outputs,
+    every consumer's bounded wait (~1 s) expires, the kernel records
+    BCJR_ERR_TIMEOUT in the workspace status word, writes NaN outputs and
+    finishes; the next normal call on the same context is correct."""
     from quant_2bit_b200 import _lib
     lib = _lib.load()
     dev = torch.device("cuda")
@@ -138,17 +130,16 @@ def test_b4_bounded_wait_timeout_is_reported_and_context_survives(cuda_ok):
     cb = torch.tensor(cb_np, device=dev)
     w = torch.tensor(w_np, device=dev)
     T = torch.tensor(0.5, device=dev)
-    soft = torch.empty_like(w)
+    soft = torch.zeros_like(w)
+    logZ = torch.zeros(2, device=dev)
     ws = _lib.workspace(2, 8, 16, 2, 2, _lib.WS_FORWARD, dev)
     P, sp = _lib.ptr, _lib.stream_ptr(dev)
-    os.environ["BCJR_B200_TEST_DROP_SENDS"] = "1"
-    try:
-        rc = lib.bcjr_fb_forward(P(w), P(cb), P(T), 2, 8, 16, 2, 2, P(soft), None,
+    with _lib.test_option(_lib.OPT_TEST_DROP_SENDS, 1):
+        rc = lib.bcjr_fb_forward(P(w), P(cb), P(T), 2, 8, 16, 2, 2, P(soft), P(logZ),
                                  P(ws), ws.numel(), sp)
-    finally:
-        del os.environ["BCJR_B200_TEST_DROP_SENDS"]
     assert rc == 0
     assert lib.bcjr_ws_status(P(ws), sp) == _lib.BCJR_ERR_TIMEOUT
+    assert torch.isnan(soft).all() and torch.isnan(logZ).all()
     s1, _, _ = _run(w_np, cb_np, 0.5, np.ones((2, 8, 2), np.float32))
     s64, _, _ = oracle.fb(w_np, cb_np, 0.5, 16, 2, 2)
     np.testing.assert_allclose(s1, s64, rtol=1e-4, atol=1e-5)

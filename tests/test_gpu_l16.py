@@ -3,7 +3,6 @@ fp64 oracle and against the generic kernel on the same inputs, over ragged
 shapes (odd B leaves one cluster slot idle, B below the cluster count, the
 shortest and longest N it serves, and N beyond it, which falls back)."""
 import ctypes
-import os
 
 import numpy as np
 import pytest
@@ -16,9 +15,8 @@ pytestmark = pytest.mark.gpu
 
 def _run(w, cb, T, grad, generic=False):
     import quant_2bit_b200 as q
-    old = os.environ.get("BCJR_B200_FORCE_GENERIC")
-    os.environ["BCJR_B200_FORCE_GENERIC"] = "1" if generic else "0"
-    try:
+    from quant_2bit_b200 import _lib
+    with _lib.test_option(_lib.OPT_FORCE_GENERIC, 1 if generic else 0):
         dev = torch.device("cuda")
         wd = torch.tensor(w, device=dev)
         cbd = torch.tensor(cb, device=dev)
@@ -26,11 +24,6 @@ def _run(w, cb, T, grad, generic=False):
         d = q.bcjr_soft_backward(wd, cbd, T, soft, torch.tensor(grad, device=dev), 16, 2, 1)
         torch.cuda.synchronize()
         return soft.cpu().numpy(), logZ.cpu().numpy(), d.cpu().numpy()
-    finally:
-        if old is None:
-            del os.environ["BCJR_B200_FORCE_GENERIC"]
-        else:
-            os.environ["BCJR_B200_FORCE_GENERIC"] = old
 
 
 @pytest.mark.parametrize("B,N,T", [(1, 2, 0.5), (3, 3, 1.0), (5, 17, 0.3), (2, 256, 0.1),
@@ -69,17 +62,13 @@ def test_cluster_kernel_many_pairs_per_cluster(cuda_ok):
     np.testing.assert_array_equal(z_all[150:153], z_sub)
 
 
-def _run_env(env, w, cb, T, g):
-    saved = {k: os.environ.get(k) for k in env}
-    os.environ.update(env)
-    try:
+def _run_clusters(size, w, cb, T, g):
+    """Forward and backward with the cluster size of both calls forced to
+    `size` (2 or 4; 0 = the automatic choice)."""
+    from quant_2bit_b200 import _lib
+    with _lib.test_option(_lib.OPT_L16_FORWARD_CLUSTER, size), \
+            _lib.test_option(_lib.OPT_L16_BACKWARD_CLUSTER, size):
         return _run(w, cb, T, g)
-    finally:
-        for k, v in saved.items():
-            if v is None:
-                del os.environ[k]
-            else:
-                os.environ[k] = v
 
 
 @pytest.mark.parametrize("B,N", [(301, 24), (160, 256), (75, 2), (80, 512)])
@@ -94,9 +83,9 @@ def test_cluster_instances_agree_bitwise(cuda_ok, B, N):
     cb = rng.standard_normal((65536, 1)).astype(np.float32)
     w = rng.standard_normal((B, N, 1)).astype(np.float32)
     g = rng.standard_normal((B, N, 1)).astype(np.float32)
-    s2, z2, d2 = _run_env({"BCJR_B200_L16_FORWARD": "2", "BCJR_B200_L16_BACKWARD": "2"}, w, cb, 0.5, g)
-    s4, z4, d4 = _run_env({"BCJR_B200_L16_FORWARD": "4", "BCJR_B200_L16_BACKWARD": "4"}, w, cb, 0.5, g)
-    sd, zd, dd = _run_env({"BCJR_B200_L16_FORWARD": "0", "BCJR_B200_L16_BACKWARD": "0"}, w, cb, 0.5, g)
+    s2, z2, d2 = _run_clusters(2, w, cb, 0.5, g)
+    s4, z4, d4 = _run_clusters(4, w, cb, 0.5, g)
+    sd, zd, dd = _run_clusters(0, w, cb, 0.5, g)
     np.testing.assert_array_equal(s2, s4)
     np.testing.assert_array_equal(z2, z4)
     np.testing.assert_array_equal(d2, d4)
@@ -127,11 +116,12 @@ def test_low_temperature_normwise(cuda_ok):
 
 
 def test_bounded_wait_timeout_is_reported_and_context_survives(cuda_ok):
-    """Failure detection without a GPU fault: with BCJR_B200_TEST_DROP_SENDS=1
-    one CTA of each cluster withholds its outputs, every consumer's bounded
-    wait (~1 s) expires, the kernel records BCJR_ERR_TIMEOUT in the workspace
-    status word and finishes; the host reads the status, and the next normal
-    call on the same context is correct."""
+    """Failure detection without a GPU fault: with the test option
+    BCJR_OPT_TEST_DROP_SENDS one CTA of each cluster withholds its outputs,
+    every consumer's bounded wait (~1 s) expires, the kernel records
+    BCJR_ERR_TIMEOUT in the workspace status word, writes NaN outputs and
+    finishes; the host reads the status, and the next normal call on the
+    same context is correct."""
     from quant_2bit_b200 import _lib
     lib = _lib.load()
     dev = torch.device("cuda")
@@ -139,17 +129,17 @@ def test_bounded_wait_timeout_is_reported_and_context_survives(cuda_ok):
     cb = torch.tensor(rng.standard_normal((65536, 1)), dtype=torch.float32, device=dev)
     w = torch.tensor(rng.standard_normal((2, 8, 1)), dtype=torch.float32, device=dev)
     T = torch.tensor(0.5, device=dev)
-    soft = torch.empty_like(w)
+    soft = torch.zeros_like(w)
+    logZ = torch.zeros(2, device=dev)
     ws = _lib.workspace(2, 8, 16, 2, 1, _lib.WS_FORWARD, dev)
     P, sp = _lib.ptr, _lib.stream_ptr(dev)
-    os.environ["BCJR_B200_TEST_DROP_SENDS"] = "1"
-    try:
-        rc = lib.bcjr_fb_forward(P(w), P(cb), P(T), 2, 8, 16, 2, 1, P(soft), None,
+    with _lib.test_option(_lib.OPT_TEST_DROP_SENDS, 1):
+        rc = lib.bcjr_fb_forward(P(w), P(cb), P(T), 2, 8, 16, 2, 1, P(soft), P(logZ),
                                  P(ws), ws.numel(), sp)
-    finally:
-        del os.environ["BCJR_B200_TEST_DROP_SENDS"]
     assert rc == 0
     assert lib.bcjr_ws_status(P(ws), sp) == _lib.BCJR_ERR_TIMEOUT
+    # the failure reaches the numbers: every output of the failed call is NaN
+    assert torch.isnan(soft).all() and torch.isnan(logZ).all()
     s1, _, _ = _run(w.cpu().numpy(), cb.cpu().numpy(), 0.5, np.ones((2, 8, 1), np.float32))
     s64, _, _ = oracle.fb(w.cpu().numpy(), cb.cpu().numpy(), 0.5, 16, 2, 1)
     np.testing.assert_allclose(s1, s64, rtol=1e-4, atol=1e-5)
@@ -169,17 +159,16 @@ def test_bounded_wait_timeout_with_two_grids(cuda_ok):
     T = torch.tensor(0.5, device=dev)
     soft = torch.rand_like(w)
     g = torch.ones_like(w)
-    d = torch.empty_like(w)
+    d = torch.zeros_like(w)
     ws = _lib.workspace(B, N, 16, 2, 1, _lib.WS_BACKWARD, dev)
     P, sp = _lib.ptr, _lib.stream_ptr(dev)
-    os.environ["BCJR_B200_TEST_DROP_SENDS"] = "1"
-    try:
+    with _lib.test_option(_lib.OPT_TEST_DROP_SENDS, 1):
         rc = lib.bcjr_fb_backward(P(w), P(cb), P(T), P(soft), P(g), B, N, 16, 2, 1, P(d),
                                   P(ws), ws.numel(), sp)
-    finally:
-        del os.environ["BCJR_B200_TEST_DROP_SENDS"]
     assert rc == 0
     assert lib.bcjr_ws_status(P(ws), sp) == _lib.BCJR_ERR_TIMEOUT
+    # every sequence, also those claimed after the failure, has NaN gradients
+    assert torch.isnan(d).all()
     wn = w[:3].cpu().numpy()
     s1, _, d1 = _run(wn, cb.cpu().numpy(), 0.5, np.ones((3, N, 1), np.float32))
     s64, _, d64 = oracle.fb(wn, cb.cpu().numpy(), 0.5, 16, 2, 1, grad_soft=np.ones((3, N, 1)))

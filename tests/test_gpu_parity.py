@@ -18,7 +18,8 @@ from oracle import oracle, torch_port
 pytestmark = pytest.mark.gpu
 
 ALL_GOLDEN = (golden_names("small_*.npz") + golden_names("c1_*.npz")
-              + golden_names("l16_*.npz") + golden_names("l16v2_*.npz"))
+              + golden_names("l16_*.npz") + golden_names("l16v2_*.npz")
+              + golden_names("c3_*.npz") + golden_names("c5_*.npz"))
 
 
 def run_ours(w, cb, T, L, k, V, grad, T_as="cuda"):
@@ -228,3 +229,73 @@ def test_full_size_config2_properties(cuda_ok):
     np.testing.assert_allclose(soft[idx].cpu().numpy(), s64, rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(d1[idx].cpu().numpy(), dd64, rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(logZ[idx].cpu().numpy(), z64, rtol=2e-6)
+
+
+@pytest.mark.parametrize("name", ["c3_scaled_T0.5.npz", "c5_scaled_T0.5.npz"])
+def test_scaled_layer_tiles_inside_a_full_batch(cuda_ok, name):
+    """Configs 3 and 5 scale the weights by U[0.5, 2] per row or per expert,
+    so |w| reaches ~6.4 at T = 0.5, a cost range the N(0,1) and Student-t
+    goldens do not reach.  The reference's outputs for the largest-scale
+    tiles of each layer, placed among 192 sequences (scale-2 fillers), so
+    that the forward runs two rounds of clusters and the L=16 backward its
+    4-CTA and 2-CTA grids side by side; elementwise against the reference's
+    fp64 and fp32 outputs at 1e-4 relative / 1e-5 absolute."""
+    d = load_golden(name)
+    rng = np.random.default_rng(77)
+    B, N = 192, d["w"].shape[1]
+    w = (2.0 * rng.standard_normal((B, N, 1))).astype(np.float32)
+    g = rng.standard_normal((B, N, 1)).astype(np.float32)
+    pos = [5, 100, 191][:d["w"].shape[0]]
+    w[pos] = d["w"]
+    g[pos] = d["grad"]
+    soft, logZ, dseq = run_ours(w, d["cb"], d["T"], 16, 2, 1, g)
+    for ours, key in ((soft[pos], "soft"), (dseq[pos], "dseq")):
+        rep = parity_report(ours, d[key + "32"], d[key + "64"])
+        assert rep["vs64"], (name, key, rep)
+        assert rep["vs32"], (name, key, rep)
+    np.testing.assert_allclose(logZ[pos], d["logZ64"], rtol=2e-6, atol=1e-4)
+    assert np.isfinite(soft).all() and np.isfinite(dseq).all()
+
+
+@pytest.mark.parametrize("L,k,V,N", [(16, 2, 1, 64), (16, 2, 2, 32), (8, 2, 1, 32)])
+@pytest.mark.parametrize("bad", [float("nan"), float("inf")])
+def test_nan_and_inf_inputs_propagate(cuda_ok, L, k, V, N, bad):
+    """NaN policy "propagate", as in the reference: one NaN (or infinite)
+    weight makes every local energy of its step NaN there, hence log Z,
+    every marginal, soft codeword and gradient entry of that sequence NaN
+    (forward_backward.py:98-103, :219-232 under IEEE arithmetic).  The other
+    sequences of the batch are unaffected, bitwise."""
+    rng = np.random.default_rng(L * 7 + V)
+    B = 4
+    cb = rng.standard_normal((1 << L, V)).astype(np.float32)
+    w = rng.standard_normal((B, N, V)).astype(np.float32)
+    g = rng.standard_normal((B, N, V)).astype(np.float32)
+    clean = run_ours(w, cb, 0.5, L, k, V, g)
+    w_bad = w.copy()
+    w_bad[1, N // 2, 0] = bad
+    out = run_ours(w_bad, cb, 0.5, L, k, V, g)
+    for a, b in zip(out, clean):
+        assert np.isnan(a[1]).all()
+        keep = [0, 2, 3]
+        np.testing.assert_array_equal(a[keep], b[keep])
+
+
+@pytest.mark.parametrize("L,k,V,N", [(16, 2, 1, 16), (16, 2, 2, 16), (6, 2, 1, 8)])
+@pytest.mark.parametrize("T", [0.0, -1.0, float("nan"), float("inf")])
+def test_unusable_device_temperature_gives_nan(cuda_ok, L, k, V, N, T):
+    """A temperature that is not positive and finite: as a python number it
+    is refused on the host (ValueError); on the device it cannot be checked
+    without a synchronisation, so every kernel writes NaN into every output
+    (soft, log Z, gradient)."""
+    import quant_2bit_b200 as q
+    rng = np.random.default_rng(3)
+    dev = torch.device("cuda")
+    cb = torch.tensor(rng.standard_normal((1 << L, V)), dtype=torch.float32, device=dev)
+    x = torch.tensor(rng.standard_normal((3, N, V)), dtype=torch.float32, device=dev,
+                     requires_grad=True)
+    soft, logZ = q.bcjr_forward_backward(x, cb, torch.tensor(T, device=dev), L=L, k=k, V=V)
+    soft.sum().backward()
+    torch.cuda.synchronize()
+    assert torch.isnan(soft).all() and torch.isnan(logZ).all() and torch.isnan(x.grad).all()
+    with pytest.raises(ValueError):
+        q.bcjr_forward_backward(x, cb, T, L=L, k=k, V=V)

@@ -53,10 +53,12 @@ def test_c_oracle_config1(name):
 
 
 @pytest.mark.parametrize("name", ["l16_gauss_T0.5.npz", "l16_t3_T0.05.npz", "l16_v2.npz",
-                                  "l16v2_gauss_T0.05.npz", "l16v2_hyb_T0.3.npz"])
+                                  "l16v2_gauss_T0.05.npz", "l16v2_hyb_T0.3.npz",
+                                  "c3_scaled_T0.5.npz", "c5_scaled_T0.5.npz"])
 def test_c_oracle_l16(name):
     """L=16 production trellis (V=1 at T=0.5 and the hardest T; V=2 at T=0.5,
-    at the hardest T, and with a HYB codebook)."""
+    at the hardest T, and with a HYB codebook; the largest-scale tiles of
+    the Llama and OLMoE layer workloads, |w| up to ~6.4)."""
     d = load_golden(name)
     soft, logZ, dseq = oracle.fb(d["w"], d["cb"], d["T"], d["L"], d["k"], d["V"],
                                  grad_soft=d["grad"], dtype=np.float64)

@@ -125,3 +125,14 @@ def test_quantize_layer_equals_per_weight(cuda_ok):
         (ref * G).sum().backward()
         assert torch.equal(o.detach(), ref.detach())
         assert torch.equal(x.grad, y.grad)
+
+
+def test_python_temperature_must_be_positive_and_finite():
+    """A python-number T is checked on the host (ValueError), with no device
+    access; a device T is checked by the kernels (NaN outputs)."""
+    import torch
+    from quant_2bit_b200 import bcjr
+    for T in (0.0, -1.0, float("nan"), float("inf"), -0.0):
+        with pytest.raises(ValueError):
+            bcjr._temperature(T, torch.device("cpu"))
+    assert float(bcjr._temperature(0.5, torch.device("cpu"))) == 0.5

@@ -98,21 +98,18 @@ def test_reference_entry_point_and_errors(cuda_ok):
 @pytest.mark.gpu
 @pytest.mark.parametrize("B,N", [(64, 128), (2049, 8), (3, 512)])
 def test_cluster_and_generic_kernels_agree(cuda_ok, B, N):
-    """L=16, k=2, V=2 runs on the 4-CTA cluster kernel; BCJR_B200_FORCE_GENERIC=1
-    sends it to the one-block-per-sequence kernel.  Both are exact: identical
-    results, across the 2048-sequence chunking of the cluster path and at the
-    longest N it serves."""
-    import os
+    """L=16, k=2, V=2 runs on the 4-CTA cluster kernel; the test option
+    BCJR_OPT_FORCE_GENERIC sends it to the one-block-per-sequence kernel.
+    Both are exact: identical results, across the 2048-sequence chunking of
+    the cluster path and at the longest N it serves."""
+    from quant_2bit_b200 import _lib
     from quant_2bit_b200.viterbi import viterbi_encode_batched
     rng = np.random.default_rng(B + N)
     cb = torch.tensor(hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32)), device="cuda")
     seqs = torch.tensor(rng.standard_normal((B, 2 * N)).astype(np.float32), device="cuda")
     a = viterbi_encode_batched(seqs, cb, 16, 2, 2)
-    os.environ["BCJR_B200_FORCE_GENERIC"] = "1"
-    try:
+    with _lib.test_option(_lib.OPT_FORCE_GENERIC, 1):
         b = viterbi_encode_batched(seqs, cb, 16, 2, 2)
-    finally:
-        del os.environ["BCJR_B200_FORCE_GENERIC"]
     for x, y in zip(a[:3], b[:3]):
         assert torch.equal(x, y)
     torch.testing.assert_close(a[3], b[3], rtol=1e-6, atol=1e-7)
@@ -120,12 +117,12 @@ def test_cluster_and_generic_kernels_agree(cuda_ok, B, N):
 
 @pytest.mark.gpu
 def test_cluster_wait_timeout_is_reported_and_context_survives(cuda_ok):
-    """Failure detection without a GPU fault: with BCJR_B200_TEST_DROP_SENDS=1
-    one CTA of each cluster withholds its group minima, every bounded wait of
-    the cluster Viterbi expires (~1 s), the status word reports
-    BCJR_ERR_TIMEOUT, the walk-back still reads in bounds, and the next
-    normal call on the same context is bit-exact."""
-    import os
+    """Failure detection without a GPU fault: with the test option
+    BCJR_OPT_TEST_DROP_SENDS one CTA of each cluster withholds its group
+    minima, every bounded wait of the cluster Viterbi expires (~1 s), the
+    status word reports BCJR_ERR_TIMEOUT, the walk-back still reads in bounds
+    and writes NaN reconstructions and MSEs, and the next normal call on the
+    same context is bit-exact."""
     from quant_2bit_b200 import _lib
     from quant_2bit_b200.viterbi import viterbi_encode_batched
     lib = _lib.load()
@@ -140,15 +137,13 @@ def test_cluster_wait_timeout_is_reported_and_context_survives(cuda_ok):
     mse = torch.empty((B,), dtype=torch.float32, device=dev)
     ws = torch.empty(lib.bcjr_viterbi_workspace_bytes(B, N, 16, 2, 2), dtype=torch.uint8, device=dev)
     P, sp = _lib.ptr, _lib.stream_ptr(dev)
-    os.environ["BCJR_B200_TEST_DROP_SENDS"] = "1"
-    try:
+    with _lib.test_option(_lib.OPT_TEST_DROP_SENDS, 1):
         rc = lib.bcjr_viterbi(P(seqs), P(cb), B, N, 16, 2, 2, P(bits), P(starts), P(rec), P(mse),
                               P(ws), ws.numel(), sp)
-    finally:
-        del os.environ["BCJR_B200_TEST_DROP_SENDS"]
     assert rc == 0
     assert lib.bcjr_ws_status(P(ws), sp) == _lib.BCJR_ERR_TIMEOUT
     assert int(starts.max()) < 65536 and int(bits.max()) < 16
+    assert torch.isnan(rec).all() and torch.isnan(mse).all()
     out = [o.cpu().numpy() for o in viterbi_encode_batched(seqs, cb, 16, 2, 2)]
     ref = viterbi.viterbi(seqs.cpu().numpy(), cb.cpu().numpy(), 16, 2, 2)
     for a, b in zip(out[:3], ref[:3]):

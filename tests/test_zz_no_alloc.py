@@ -5,8 +5,11 @@ allocator, or a loop that must not call cudaMalloc between steps).
 It runs on a fixed scratch array inside the library instead of a caller
 workspace; this checks, through the C ABI, that two calls in a row give the
 same soft codewords and log Z as bcjr_fb_forward within the parity tolerance
-(1e-4 relative, 1e-5 absolute), and that a shape too large for the fixed
-scratch is refused.  Kept in its own file, collected last."""
+(1e-4 relative, 1e-5 absolute) -- including batches with more sequences than
+the scratch has slots, where a block takes its next sequence on the slot
+its last one left behind, and the longest sequence that fits -- and that a
+shape too large for the fixed scratch is refused.  Kept in its own file,
+collected last."""
 import numpy as np
 import pytest
 import torch
@@ -15,7 +18,11 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("L,k,V,N,B,T", [(8, 2, 1, 256, 64, 1.0), (16, 2, 1, 64, 5, 0.5),
-                                         (10, 2, 2, 40, 7, 0.7)])
+                                         (10, 2, 2, 40, 7, 0.7),
+                                         # one 33.8 MB slot fits: 4 sequences on one block
+                                         (16, 2, 1, 512, 4, 0.5),
+                                         # the longest sequence whose slot fits at L=16, k=2, V=1
+                                         (16, 2, 1, 1020, 1, 0.5)])
 def test_noalloc_forward_matches_forward(cuda_ok, L, k, V, N, B, T):
     from quant_2bit_b200 import _lib
     lib = _lib.load()
@@ -41,15 +48,18 @@ def test_noalloc_forward_matches_forward(cuda_ok, L, k, V, N, B, T):
         np.testing.assert_allclose(logZ.cpu().numpy(), ref_logZ.cpu().numpy(), rtol=2e-6, atol=1e-4)
 
 
-def test_noalloc_rejects_shapes_beyond_the_scratch(cuda_ok):
+@pytest.mark.parametrize("N", [1021, 4096])
+def test_noalloc_rejects_shapes_beyond_the_scratch(cuda_ok, N):
+    """One slot of (N + 3) 2^14 + 2N floats must fit the 64 MiB scratch:
+    N = 1021 and longer are refused before any launch."""
     from quant_2bit_b200 import _lib
     lib = _lib.load()
     dev = torch.device("cuda", 0)
-    w = torch.zeros((1, 4096, 1), device=dev)
+    w = torch.zeros((1, N, 1), device=dev)
     cb = torch.zeros((65536, 1), device=dev)
     Tt = torch.tensor(1.0, device=dev)
     soft = torch.empty_like(w)
-    rc = lib.bcjr_fb_forward_noalloc(_lib.ptr(w), _lib.ptr(cb), _lib.ptr(Tt), 1, 4096, 16, 2, 1,
+    rc = lib.bcjr_fb_forward_noalloc(_lib.ptr(w), _lib.ptr(cb), _lib.ptr(Tt), 1, N, 16, 2, 1,
                                      _lib.ptr(soft), None, _lib.stream_ptr(dev))
     BCJR_ERR_WORKSPACE = 5
     assert rc == BCJR_ERR_WORKSPACE
