@@ -575,11 +575,15 @@ def run_bcjr(args, rank, world, local_rank):
     EDGES_PER_SEQ = NSTEP * (1 << L) * (1 << (K_BITS * V))
     STATE_STEPS_PER_SEQ = NSTEP * (1 << L)
     MUFU_FWD, MUFU_BWD = MUFU[V]
+    if args.gather_sms is not None:
+        qd.GATHER_RESERVED_SMS = args.gather_sms
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        # NCCL capped to the SMs the kernels leave free while gathers overlap them
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300),
+                                pg_options=qd.nccl_options(qd.GATHER_RESERVED_SMS))
 
     cb_cpu, w_cpu, total_seqs = make_inputs(args.config, rank, world, args.weights)
     if args.config in ("c3", "c5") and not args.sequences:
@@ -608,7 +612,9 @@ def run_bcjr(args, rank, world, local_rank):
         soft, handle = qd.layer_forward(w, shards, cb, T, L, K_BITS, V, gather=do_gather)
         if ev:
             ev[1].record(stream)
-        d = qd.layer_backward(w, soft, grad, cb, T, L, K_BITS, V)
+        # the last gathers may still run beside the backward
+        d = qd.layer_backward(w, soft, grad, cb, T, L, K_BITS, V,
+                              reserve_sms=qd.GATHER_RESERVED_SMS if do_gather else 0)
         if ev:
             ev[2].record(stream)
         handle.wait()
@@ -737,7 +743,8 @@ def run_bcjr(args, rank, world, local_rank):
         if gather:
             collective = ("NCCL all_gather_into_tensor per weight on a side stream, each behind "
                           "its weight's forward launch (overlapped with the next weights' "
-                          "kernels and the backward)")
+                          f"kernels and the backward, which leave {qd.GATHER_RESERVED_SMS} SMs "
+                          f"free; NCCL capped to {qd.GATHER_RESERVED_SMS} CTAs)")
         else:
             collective = "none"
         result = {
@@ -811,6 +818,9 @@ def main():
     ap.add_argument("--sequences", type=int, default=0,
                     help="use only this many sequences per GPU (small cases for ncu)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gather-sms", type=int, default=None,
+                    help="SMs left free for the all-gathers at N > 1 (default: "
+                         "quant_2bit_b200.distributed.GATHER_RESERVED_SMS)")
     args = ap.parse_args()
 
     V, NSTEP = SHAPES[args.config]

@@ -89,6 +89,18 @@ enum {
 };
 BCJR_API int bcjr_set_test_option(int option, int value);
 
+/* SMs that the persistent cluster kernels leave free, process-wide, 0 by
+ * default (0..64).  A persistent kernel holds every SM it is given until it
+ * ends; a collective kernel queued beside it (an NCCL all-gather of a soft
+ * weight while the next weight is quantized) then waits for SMs, and one
+ * that started on one GPU spins until its peers' copies start.  Reserving a
+ * few SMs, and capping the collective's CTAs to them (NCCL_MAX_CTAS), lets
+ * both run at once.  Workspace sizes depend on it: set it before
+ * bcjr_workspace_bytes and keep it until the call is launched.  Returns the
+ * previous value, or -1 when out of range.  No counterpart in the reference
+ * (it has no multi-GPU path). */
+BCJR_API int bcjr_set_reserved_sms(int sms);
+
 /* Static string for a status code. */
 BCJR_API const char *bcjr_status_string(int status);
 

@@ -36,6 +36,7 @@ _SZ = ctypes.c_size_t
 SIGNATURES = {
     "bcjr_version": ([], _I),
     "bcjr_set_test_option": ([_I, _I], _I),
+    "bcjr_set_reserved_sms": ([_I], _I),
     "bcjr_status_string": ([_I], ctypes.c_char_p),
     "bcjr_workspace_bytes": ([_I, _I, _I, _I, _I, _I], _SZ),
     "bcjr_check_shape": ([_I, _I, _I, _I, _I], _I),
@@ -110,6 +111,21 @@ def test_option(option, value):
         yield
     finally:
         lib.bcjr_set_test_option(option, old)
+
+
+@contextlib.contextmanager
+def reserved_sms(n):
+    """Leave `n` SMs free of the persistent cluster kernels for the duration
+    of a block (bcjr_set_reserved_sms), e.g. for collectives that overlap
+    them."""
+    lib = load()
+    old = lib.bcjr_set_reserved_sms(int(n))
+    if old < 0:
+        raise ValueError(f"reserved SMs must be in 0..64, got {n}")
+    try:
+        yield
+    finally:
+        lib.bcjr_set_reserved_sms(old)
 
 
 def ptr(t):

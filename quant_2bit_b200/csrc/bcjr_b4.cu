@@ -723,7 +723,13 @@ bool b4_applicable(int B, int N, int L, int BB, int V) {
 }
 
 int b4_clusters(int B, int mode) {
-    const int maxc = (mode == kModeBackward) ? b4_max_clusters<true>() : b4_max_clusters<false>();
+    int maxc = (mode == kModeBackward) ? b4_max_clusters<true>() : b4_max_clusters<false>();
+    // SMs left free for concurrent kernels (bcjr_set_reserved_sms)
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int cap = (sms - reserved_sms()) / b4::kCL;
+    if (maxc > cap) maxc = cap;
     const long pairs = ((long)B + b4::kSlots - 1) / b4::kSlots;
     long n = maxc;
     if (n > pairs) n = pairs;

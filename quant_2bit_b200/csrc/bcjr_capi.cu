@@ -15,11 +15,14 @@ namespace bcjr {
 
 namespace {
 std::atomic<int> g_test_options[kOptCount];
+std::atomic<int> g_reserved_sms{0};
 }  // namespace
 
 int test_option(int which) {
     return (which > 0 && which < kOptCount) ? g_test_options[which].load(std::memory_order_relaxed) : 0;
 }
+
+int reserved_sms() { return g_reserved_sms.load(std::memory_order_relaxed); }
 
 }  // namespace bcjr
 
@@ -155,6 +158,11 @@ int bcjr_version(void) { return 200; }
 int bcjr_set_test_option(int option, int value) {
     if (option <= 0 || option >= bcjr::kOptCount) return -1;
     return bcjr::g_test_options[option].exchange(value);
+}
+
+int bcjr_set_reserved_sms(int sms) {
+    if (sms < 0 || sms > 64) return -1;
+    return bcjr::g_reserved_sms.exchange(sms);
 }
 
 const char *bcjr_status_string(int status) {

@@ -181,12 +181,17 @@ __device__ __forceinline__ float order_key_inv(int k) {
 }
 
 // Soft-min accumulator (m, s): value = m - lg2 s, s = sum 2^(m - x).
+// A NaN partial makes the result NaN (NaN policy "propagate": a sequence
+// with a NaN energy has a NaN log Z, hence NaN marginals, as in the
+// reference); +inf partials (empty) are skipped.
 __device__ __forceinline__ void smin_merge(float &m, float &s, float m2, float s2) {
     if (m2 < m) {
         s = s * ex2(m2 - m) + s2;
         m = m2;
     } else if (m2 < kPosInf) {
         s = s + s2 * ex2(m - m2);
+    } else if (m2 != m2) {
+        m = m2;
     }
 }
 

@@ -108,13 +108,16 @@ __device__ __forceinline__ void block_sum(float (&v)[NV], float *sh) {
     for (int i = 0; i < NV; ++i) v[i] = sh[nw * NV + i];
 }
 
-// Merge two (max, sum-of-2^(x-max)) pairs.
+// Merge two (max, sum-of-2^(x-max)) pairs.  A NaN partial makes the result
+// NaN (NaN policy "propagate"); -inf partials (empty) are skipped.
 __device__ __forceinline__ void lse_merge(float &m, float &s, float m2, float s2) {
     if (m2 > m) {
         s = s * ex2(m - m2) + s2;
         m = m2;
     } else if (m2 > kNegInf) {
         s = s + s2 * ex2(m2 - m);
+    } else if (m2 != m2) {
+        m = m2;
     }
 }
 

@@ -18,6 +18,9 @@ enum {
     kOptCount = 5
 };
 int test_option(int which);   // bcjr_capi.cu
+// SMs the cluster kernels leave free for concurrent kernels (collectives),
+// set through bcjr_set_reserved_sms() (C ABI); 0 by default.
+int reserved_sms();           // bcjr_capi.cu
 enum { kKernelGeneric = 0, kKernelL16 = 1, kKernelB4 = 2 };
 
 struct LaunchArgs {

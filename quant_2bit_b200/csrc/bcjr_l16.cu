@@ -794,9 +794,16 @@ Plan plan_for(int B, int mode) {
     const long b = B > 0 ? B : 1;
     const bool bwd = mode == kModeBackward;
     const int force = test_option(bwd ? kOptL16Backward : kOptL16Forward);
-    const int max2 = l16::max_clusters(mode);
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // SMs left free for concurrent kernels (bcjr_set_reserved_sms)
+    const int free_sms = sms - reserved_sms();
+    int max2 = l16::max_clusters(mode);
+    if (max2 > free_sms / 2) max2 = free_sms / 2;
     const long need2 = (b + l16::slots(mode) - 1) / l16::slots(mode);
-    const int max4 = l16c4::max_clusters(mode);
+    int max4 = l16c4::max_clusters(mode);
+    if (max4 > free_sms / 4) max4 = free_sms / 4;
     const long need4 = (b + l16c4::slots(mode) - 1) / l16c4::slots(mode);
     if (force == 4 && max4 > 0) {
         p.n4 = (int)(need4 < max4 ? need4 : max4);
@@ -806,13 +813,11 @@ Plan plan_for(int B, int mode) {
     // the 2-CTA instance alone
     if (!bwd || force == 2 || max4 <= 0 || need2 <= max2) {
         p.n2 = (int)(need2 < max2 ? need2 : max2);
+        if (p.n2 < 0) p.n2 = 0;
         return p;
     }
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     p.n4 = max4;
-    p.n2 = (sms - 4 * max4) / 2;
+    p.n2 = (free_sms - 4 * max4) / 2;
     if (p.n2 < 0) p.n2 = 0;
     return p;
 }

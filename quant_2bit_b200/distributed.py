@@ -17,11 +17,16 @@ Two ways to split, both in ``LayerShards``:
 * whole weights (``owners``): each weight lives on one rank, e.g. the
   experts of an MoE layer, a few per GPU; nothing is reassembled.
 
-``layer_forward`` launches one forward per weight on the current stream and
-queues that weight's all-gather on a side stream behind an event, so the
-gather of weight i overlaps the kernels of weight i + 1 and of whatever the
-caller queues next (the backward); ``GatherHandle.wait()`` orders the
-current stream after the gathers, with no host synchronisation.
+``layer_forward`` launches one forward per weight on the current stream
+(largest weights first) and queues that weight's all-gather on a side stream
+behind an event, so the gather of weight i overlaps the kernels of the next
+weights and of whatever the caller queues next (the backward);
+``GatherHandle.wait()`` orders the current stream after the gathers, with
+no host synchronisation.  The persistent kernels hold every SM they are
+given, and an NCCL kernel that waits for SMs on one GPU stalls its peers, so
+while gathers are in flight the kernels leave ``GATHER_RESERVED_SMS`` SMs
+free (bcjr_set_reserved_sms) and NCCL is capped to as many CTAs
+(``nccl_options``).
 
 Gradients.  Every rank's loss depends on every soft weight, so the gradient
 of the summed loss with respect to rank r's tiles needs the SUM over ranks
@@ -38,10 +43,31 @@ reassembly.  ``compute`` lets tests substitute a CPU function for the
 kernels (gloo ranks on CPU); the default is the sm_100a kernels, with no CPU
 fallback.
 """
+import contextlib
+
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from . import bcjr as _bcjr
+
+# SMs left free of the cluster kernels while all-gathers overlap them, and the
+# CTA cap of the NCCL communicator that runs the gathers.
+GATHER_RESERVED_SMS = 8
+
+
+def nccl_options(max_ctas=GATHER_RESERVED_SMS):
+    """ProcessGroupNCCL options whose collectives use at most ``max_ctas``
+    CTAs (also for NVLS), so that they fit the SMs the kernels leave free:
+    ``dist.init_process_group("nccl", pg_options=nccl_options(), ...)``."""
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.config.max_ctas = int(max_ctas)
+    opts.config.nvls_ctas = int(max_ctas)
+    return opts
+
+
+def _reserve(n, cuda):
+    return _lib.reserved_sms(n) if (cuda and n) else contextlib.nullcontext()
 
 
 def shard_range(B, world, rank):
@@ -176,15 +202,17 @@ class GatherHandle:
 
 
 def layer_forward(local_seqs, shards, codebook, T_temp, L=16, k=2, V=1, group=None,
-                  gather=True, compute=None):
+                  gather=True, compute=None, reserve_sms=None):
     """Soft codewords of this rank's sequences, weight by weight.
 
     Returns ``(soft_local, handle)``: ``soft_local`` is (shards.local, N, V)
     in the order of ``local_seqs``; ``handle.gathered[i]`` becomes the full
     (counts[i], N, V) soft weight i once ``handle.wait()`` has been called
     (split shards with ``gather``; None otherwise).  One kernel launch per
-    weight on the current stream; on CUDA each weight's all-gather runs on a
-    side stream after an event recorded behind its launch."""
+    weight on the current stream, largest first; on CUDA each weight's
+    all-gather runs on a side stream after an event recorded behind its
+    launch, with ``reserve_sms`` SMs (default ``GATHER_RESERVED_SMS``) left
+    free of the kernels for it."""
     assert local_seqs.dim() == 3 and local_seqs.shape[0] == shards.local, \
         "local_seqs must hold this rank's sequences of every weight"
     fwd = compute[0] if compute else None
@@ -206,15 +234,20 @@ def layer_forward(local_seqs, shards, codebook, T_temp, L=16, k=2, V=1, group=No
                 _bcjr.bcjr_soft_forward(local_seqs, codebook, T_temp, L, k, V, out=soft_local,
                                         want_logZ=False)
         return soft_local, GatherHandle(gathered, None, pads)
-    for i in range(len(shards.counts)):
+    if reserve_sms is None:
+        reserve_sms = GATHER_RESERVED_SMS
+    # largest weights first: the gathers still running at the end are small
+    order = sorted(range(len(shards.counts)), key=lambda i: -shards.counts[i])
+    for i in order:
         sl = shards.local_slice(i)
         n = sl.stop - sl.start
         if n > 0:
             if compute:
                 soft_local[sl] = fwd(local_seqs[sl], codebook, T_temp, L, k, V)
             else:     # the kernel writes straight into this weight's rows
-                _bcjr.bcjr_soft_forward(local_seqs[sl], codebook, T_temp, L, k, V,
-                                        out=soft_local[sl], want_logZ=False)
+                with _reserve(reserve_sms, cuda):
+                    _bcjr.bcjr_soft_forward(local_seqs[sl], codebook, T_temp, L, k, V,
+                                            out=soft_local[sl], want_logZ=False)
         B, per = shards.counts[i], shards.padded(i)
         buf = torch.empty((per * shards.world, N, V), dtype=torch.float32, device=local_seqs.device)
         src = soft_local[sl]
@@ -237,13 +270,16 @@ def layer_forward(local_seqs, shards, codebook, T_temp, L=16, k=2, V=1, group=No
 
 
 def layer_backward(local_seqs, soft_local, grad_local, codebook, T_temp, L=16, k=2, V=1,
-                   compute=None):
+                   compute=None, reserve_sms=0):
     """Gradient with respect to this rank's sequences (one launch for all of
-    them), given the upstream gradient rows of the same sequences."""
+    them), given the upstream gradient rows of the same sequences.  Pass
+    ``reserve_sms`` (e.g. ``GATHER_RESERVED_SMS``) when gathers of a
+    ``layer_forward`` are still in flight."""
     bwd = compute[1] if compute else _default_backward
     if local_seqs.shape[0] == 0:
         return torch.zeros_like(local_seqs)
-    return bwd(local_seqs, codebook, T_temp, soft_local, grad_local.contiguous(), L, k, V)
+    with _reserve(reserve_sms, local_seqs.is_cuda and not compute):
+        return bwd(local_seqs, codebook, T_temp, soft_local, grad_local.contiguous(), L, k, V)
 
 
 def local_grad_rows(grads, shards, group=None, grad_reduce=True):
