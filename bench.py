@@ -560,8 +560,8 @@ def run_viterbi(args, rank, world, local_rank):
 # measured by ncu (sm__pipe_fma_cycles_active.sum over one launch / the
 # launch's state-steps; profiles/): the basis of the FP32-issue fraction in
 # the bench line, next to the MUFU fraction.
-FMA_CYCLES_PER_STATE_STEP = {1: {"forward": 0.0956, "backward": 0.1985},
-                             2: {"forward": None, "backward": None}}
+FMA_CYCLES_PER_STATE_STEP = {1: {"forward": 0.0963, "backward": 0.1944},
+                             2: {"forward": 0.1349, "backward": 0.2337}}
 
 
 def run_bcjr(args, rank, world, local_rank):

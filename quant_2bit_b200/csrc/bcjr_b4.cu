@@ -408,22 +408,23 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     }
                     const float m = min16(x);
                     const F2 KM = bc(kap * m);
+                    // each pair's dependent FMA work right after its two ex2,
+                    // so the MUFU and FMA pipes interleave (same sums, same order)
                     F2 e[8];
+                    F2 hf = bc(0.f);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) e[i] = ex2p(fma2(x[i], NK, KM));
-                    const F2 S2 = sum8(e);
-                    const float S = S2.x + S2.y;
-                    o[h][rr] = fmaf(-lg2(S), ikap, m - sub);
-                    if (GRAD) {
-                        F2 hf = bc(0.f);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
+                    for (int i = 0; i < 8; ++i) {
+                        e[i] = ex2p(fma2(x[i], NK, KM));
+                        if (GRAD) {
                             const F2 H = *reinterpret_cast<const F2 *>(in + kIn + 2 * (i * kRPC + rl));
                             const F2 f = fma2(C0[h][rr][i], G0, fma2(C1[h][rr][i], G1, sub2(H, GS)));
                             hf = fma2(e[i], f, hf);
                         }
-                        hh[h][rr] = (hf.x + hf.y) * rcp(S);
                     }
+                    const F2 S2 = sum8(e);
+                    const float S = S2.x + S2.y;
+                    o[h][rr] = fmaf(-lg2(S), ikap, m - sub);
+                    if (GRAD) hh[h][rr] = (hf.x + hf.y) * rcp(S);
                 }
                 lmin = min3(lmin, o[h][0], o[h][1]);
                 if (!last) {
@@ -585,28 +586,20 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     }
                     const float m = min16(x);
                     const F2 KM = bc(kap * m);
-                    F2 e[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) e[i] = ex2p(fma2(x[i], NK, KM));
-                    const F2 S2 = sum8(e);
-                    const float S = S2.x + S2.y;
                     const float ms = m - sigma;
-                    ob[h][rr] = t >= 0 ? fmaf(-lg2(S), ikap, ms) : 0.f;
                     const float f = ex2(fmaf(ms + ah[h][rr], -kap, Cb));
-                    if (!GRAD) {
-                        F2 e0 = mul2(e[0], C0[h][rr][0]), e1 = mul2(e[0], C1[h][rr][0]);
+                    // as in the alpha sweep: each pair's accumulations right after its ex2
+                    F2 e[8];
+                    F2 e0 = bc(0.f), e1 = bc(0.f);
+                    const F2 HP = bc(GRAD ? hp[h][rr] : 0.f);
+                    F2 ey = bc(0.f), sv = bc(0.f), s0 = bc(0.f), s1 = bc(0.f);
 #pragma unroll
-                        for (int i = 1; i < 8; ++i) {
-                            e0 = fma2(e[i], C0[h][rr][i], e0);
-                            e1 = fma2(e[i], C1[h][rr][i], e1);
-                        }
-                        acc = fma2(bc(f), mk(e0.x + e0.y, e1.x + e1.y), acc);
-                        bbo[h][rr] = 0.f;
-                    } else {
-                        const F2 HP = bc(hp[h][rr]);
-                        F2 ey = bc(0.f), sv = bc(0.f), s0 = bc(0.f), s1 = bc(0.f);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
+                    for (int i = 0; i < 8; ++i) {
+                        e[i] = ex2p(fma2(x[i], NK, KM));
+                        if (!GRAD) {
+                            e0 = i == 0 ? mul2(e[0], C0[h][rr][0]) : fma2(e[i], C0[h][rr][i], e0);
+                            e1 = i == 0 ? mul2(e[0], C1[h][rr][0]) : fma2(e[i], C1[h][rr][i], e1);
+                        } else {
                             const F2 y = fma2(C0[h][rr][i], G0, fma2(C1[h][rr][i], G1, bbin[i]));
                             ey = fma2(e[i], y, ey);
                             const F2 v = mul2(e[i], add2(y, HP));
@@ -614,6 +607,14 @@ b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                             s0 = fma2(v, C0[h][rr][i], s0);
                             s1 = fma2(v, C1[h][rr][i], s1);
                         }
+                    }
+                    const F2 S2 = sum8(e);
+                    const float S = S2.x + S2.y;
+                    ob[h][rr] = t >= 0 ? fmaf(-lg2(S), ikap, ms) : 0.f;
+                    if (!GRAD) {
+                        acc = fma2(bc(f), mk(e0.x + e0.y, e1.x + e1.y), acc);
+                        bbo[h][rr] = 0.f;
+                    } else {
                         bbo[h][rr] = (ey.x + ey.y) * rcp(S);
                         const float SV = sv.x + sv.y;
                         acc = fma2(bc(f), mk(fmaf(-st.x, SV, s0.x + s0.y), fmaf(-st.y, SV, s1.x + s1.y)),
