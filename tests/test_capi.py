@@ -103,3 +103,18 @@ def test_test_options_are_set_through_the_abi_not_the_environment(lib):
     for name in os.listdir(csrc):
         text = open(os.path.join(csrc, name)).read()
         assert "getenv" not in text, name
+
+
+def test_reserved_sms_setter(lib):
+    """bcjr_set_reserved_sms: process-wide, 0 by default, 0..64, returns the
+    previous value (host-only; no GPU call)."""
+    from quant_2bit_b200 import _lib
+    assert lib.bcjr_set_reserved_sms(0) == 0
+    with _lib.reserved_sms(8):
+        assert lib.bcjr_set_reserved_sms(8) == 8
+    assert lib.bcjr_set_reserved_sms(0) == 0
+    assert lib.bcjr_set_reserved_sms(-1) == -1
+    assert lib.bcjr_set_reserved_sms(65) == -1
+    with pytest.raises(ValueError):
+        with _lib.reserved_sms(100):
+            pass

@@ -241,3 +241,34 @@ def test_graph_capture_replays_forward_and_backward(cuda_ok):
     for a, b in zip(got, want):
         assert torch.equal(a, b)
     del graph
+
+
+@pytest.mark.parametrize("V,N,B", [(1, 64, 300), (2, 32, 200)])
+def test_reserved_sms_leave_results_unchanged(cuda_ok, V, N, B):
+    """Leaving SMs free for collectives (bcjr_set_reserved_sms) shrinks the
+    cluster grids and the workspace, and changes nothing in the results:
+    bitwise the same soft codewords, log Z and gradient (each sequence is
+    computed by one cluster, in a fixed order of operations).  The 4-CTA
+    grids use 132 of 148 SMs, so a reserve of up to 16 leaves them as they
+    are; 24 shrinks every grid (and drops the L=16 backward's 2-CTA grid)."""
+    import quant_2bit_b200 as q
+    from quant_2bit_b200 import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(31 + V)
+    dev = torch.device("cuda")
+    cb = torch.tensor(rng.standard_normal((65536, V)), dtype=torch.float32, device=dev)
+    w = torch.tensor(rng.standard_normal((B, N, V)), dtype=torch.float32, device=dev)
+    g = torch.tensor(rng.standard_normal((B, N, V)), dtype=torch.float32, device=dev)
+    outs = []
+    sizes = []
+    for r in (0, 8, 24):
+        with _lib.reserved_sms(r):
+            sizes.append(lib.bcjr_workspace_bytes(B, N, 16, 2, V, _lib.WS_FORWARD | _lib.WS_BACKWARD))
+            soft, logZ = q.bcjr_soft_forward(w, cb, 0.5, 16, 2, V)
+            d = q.bcjr_soft_backward(w, cb, 0.5, soft, g, 16, 2, V)
+        torch.cuda.synchronize()
+        outs.append((soft.cpu(), logZ.cpu(), d.cpu()))
+    assert sizes[0] >= sizes[1] >= sizes[2] and sizes[0] > sizes[2]
+    for o in outs[1:]:
+        for a, b in zip(o, outs[0]):
+            assert torch.equal(a, b)
