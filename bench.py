@@ -607,17 +607,17 @@ def run_bcjr(args, rank, world, local_rank):
     last = {}
 
     def step(ev=None, do_gather=gather):
+        # forward launches (each weight's gather overlapping the next weights'
+        # kernels), then the wait for the gathers, then the backward on all SMs
         if ev:
             ev[0].record(stream)
         soft, handle = qd.layer_forward(w, shards, cb, T, L, K_BITS, V, gather=do_gather)
         if ev:
             ev[1].record(stream)
-        # the last gathers may still run beside the backward
-        d = qd.layer_backward(w, soft, grad, cb, T, L, K_BITS, V,
-                              reserve_sms=qd.GATHER_RESERVED_SMS if do_gather else 0)
+        handle.wait()
         if ev:
             ev[2].record(stream)
-        handle.wait()
+        d = qd.layer_backward(w, soft, grad, cb, T, L, K_BITS, V)
         if ev:
             ev[3].record(stream)
         last["soft"], last["d"] = soft, d
@@ -649,8 +649,8 @@ def run_bcjr(args, rank, world, local_rank):
 
     step_ms = [e[0].elapsed_time(e[3]) for e in events]
     fwd_ms = [e[0].elapsed_time(e[1]) for e in events]
-    bwd_ms = [e[1].elapsed_time(e[2]) for e in events]
-    tail_ms = [e[2].elapsed_time(e[3]) for e in events]
+    tail_ms = [e[1].elapsed_time(e[2]) for e in events]     # gathers still running after the forward
+    bwd_ms = [e[2].elapsed_time(e[3]) for e in events]
     t = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -742,9 +742,10 @@ def run_bcjr(args, rank, world, local_rank):
     if rank == 0:
         if gather:
             collective = ("NCCL all_gather_into_tensor per weight on a side stream, each behind "
-                          "its weight's forward launch (overlapped with the next weights' "
-                          f"kernels and the backward, which leave {qd.GATHER_RESERVED_SMS} SMs "
-                          f"free; NCCL capped to {qd.GATHER_RESERVED_SMS} CTAs)")
+                          "its weight's forward launch and overlapped with the next weights' "
+                          f"kernels, which leave {qd.GATHER_RESERVED_SMS} SMs free (NCCL capped "
+                          f"to {qd.GATHER_RESERVED_SMS} CTAs); the backward follows the gathers "
+                          "on all SMs")
         else:
             collective = "none"
         result = {

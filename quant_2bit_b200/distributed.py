@@ -20,13 +20,14 @@ Two ways to split, both in ``LayerShards``:
 ``layer_forward`` launches one forward per weight on the current stream
 (largest weights first) and queues that weight's all-gather on a side stream
 behind an event, so the gather of weight i overlaps the kernels of the next
-weights and of whatever the caller queues next (the backward);
-``GatherHandle.wait()`` orders the current stream after the gathers, with
-no host synchronisation.  The persistent kernels hold every SM they are
-given, and an NCCL kernel that waits for SMs on one GPU stalls its peers, so
-while gathers are in flight the kernels leave ``GATHER_RESERVED_SMS`` SMs
-free (bcjr_set_reserved_sms) and NCCL is capped to as many CTAs
-(``nccl_options``).
+weights; ``GatherHandle.wait()`` orders the current stream after the
+gathers, with no host synchronisation.  Measured on 2 to 8 B200s, the
+gathers of a Llama-3.2-1B layer finish within its forward, so the backward
+is best queued after ``wait()``, on all SMs (as ``ShardedLayerBcjr`` does).
+The persistent kernels hold every SM they are given, and an NCCL kernel that
+waits for SMs on one GPU stalls its peers, so while gathers are in flight
+the kernels leave ``GATHER_RESERVED_SMS`` SMs free (bcjr_set_reserved_sms)
+and NCCL is capped to as many CTAs (``nccl_options``).
 
 Gradients.  Every rank's loss depends on every soft weight, so the gradient
 of the summed loss with respect to rank r's tiles needs the SUM over ranks
