@@ -87,7 +87,10 @@ constexpr int kNJ = kG >> kB;         // 4096 butterflies
 constexpr int kCL = BCJR_L16_CL;      // CTAs per cluster (4 or 2)
 constexpr int kJPC = kNJ / kCL;       // butterflies per CTA
 constexpr int kIn = 4 * kJPC;         // inputs per CTA per step and plane
-constexpr int kNT = 512;              // threads per CTA
+#ifndef BCJR_L16_NT
+#define BCJR_L16_NT 512
+#endif
+constexpr int kNT = BCJR_L16_NT;      // threads per CTA
 constexpr int kJPT = kJPC / kNT;      // butterflies per thread
 static_assert(kCL == 2 || kCL == 4, "cluster of 2 or 4 CTAs");
 // Sequences in flight per cluster, interleaved step by step: two, except in
@@ -109,15 +112,32 @@ struct SleepOf {
     static constexpr unsigned value = SlotsOf<GRAD>::value == 1 ? BCJR_L16_SLEEP1_NS : kWaitSleepNs;
 };
 constexpr int kWarps = kNT / 32;
+// Virtual warps: the reductions below group butterflies as a 512-thread CTA
+// would (32 lanes x 2 butterflies 512 apart per partial), whatever kNT is,
+// so that every instance reduces in the same order.
+constexpr int kVW = 16;
 // Reduction blocks: the per-step sums (soft codewords, gradients) and log Z
-// are reduced per block of 1024 butterflies and warp, then over the 4 x 16
-// (block, warp) partials in a fixed order.  A thread's butterflies
-// tid + 512 jj fall in block (rank kJPC + 512 jj) / 1024, two per block, in
-// both instances, so a sequence's results are bitwise the same whichever
-// instance runs it.
+// are reduced per (block of 1024 butterflies, virtual warp), then over the
+// 4 x 16 partials in a fixed order.  Partial (b, v) holds butterflies
+// b 1024 + 32 v + lane + 512 h (h = 0, 1), summed per lane in the order
+// h = 0, 1 and then over the lanes; butterfly pair q = jj / 2 of a thread is
+// partial number q kWarps + warp of its CTA (jl_of below).  Every instance
+// forms the same 64 partials, so a sequence's results are bitwise the same
+// whichever instance runs it.
 constexpr int kRB = kNJ / 1024;       // 4 reduction blocks
-constexpr int kParts = kRB * kWarps;  // 64 partials per step
-static_assert(kJPT % 2 == 0, "two butterflies of a thread per reduction block");
+constexpr int kParts = kRB * kVW;     // 64 partials per step
+static_assert(kJPT % 2 == 0, "two butterflies of a thread per reduction partial");
+static_assert((kJPC / 64) % kWarps == 0, "whole partials per warp");
+
+// Local butterfly of the thread's jj-th slot, and its reduction partial.
+__device__ __forceinline__ int jl_of(int tid, int jj) {
+    const int q = (jj >> 1) * kWarps + (tid >> 5);       // partial within the CTA
+    return (q / kVW) * 1024 + 32 * (q % kVW) + (tid & 31) + 512 * (jj & 1);
+}
+__device__ __forceinline__ int part_of(uint32_t rank, int tid, int jj) {
+    const int q = (jj >> 1) * kWarps + (tid >> 5);
+    return ((int)rank * (kJPC / 1024) + q / kVW) * kVW + q % kVW;
+}
 
 template <bool GRAD>
 struct alignas(128) Smem {
@@ -204,7 +224,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     F2 cq[kJPT][4][2];
 #pragma unroll
     for (int jj = 0; jj < kJPT; ++jj) {
-        jg[jj] = (int)rank * kJPC + tid + kNT * jj;
+        jg[jj] = (int)rank * kJPC + jl_of(tid, jj);
         const float *q = cb + 4 * jg[jj];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -410,7 +430,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                     // costs of A_t minus the global minimum, and H_t, of my butterfly
                     float ain[4] = {0.f, 0.f, 0.f, 0.f}, hin[4] = {0.f, 0.f, 0.f, 0.f};
                     if (in) {
-                        const int jl = tid + kNT * jj;
+                        const int jl = jl_of(tid, jj);
 #pragma unroll
                         for (int p = 0; p < 4; ++p) {
                             ain[p] = in[p * kJPC + jl] - shift;
@@ -464,7 +484,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
                                 smin_merge(m, s, m2, s2);
                             }
                             if (lane == 0) {
-                                const int part = ((int)rank * (kJPC / 1024) + (jj >> 1)) * kWarps + warp;
+                                const int part = part_of(rank, tid, jj);
 #pragma unroll
                                 for (int r = 0; r < kCL; ++r) {
                                     st_cluster(cbase[r] + soff(&sm.lz[z][part][0]), m);
@@ -547,7 +567,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
                 for (int jj = 0; jj < kJPT; ++jj) {
                     const int j = jg[jj];
-                    const int jl = tid + kNT * jj;
+                    const int jl = jl_of(tid, jj);
                     if ((jj & 1) == 0) acc = bc(0.f);   // first butterfly of a reduction block
                     // my butterfly's inputs (minus the global minimum) and history values
                     float bin[4] = {0.f, 0.f, 0.f, 0.f}, bbin[4] = {0.f, 0.f, 0.f, 0.f};
@@ -636,8 +656,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                         if (lane == 0)
-                            slot_ws[z][lay.part + (long)tn * kParts +
-                                       ((int)rank * (kJPC / 1024) + (jj >> 1)) * kWarps + warp] = v;
+                            slot_ws[z][lay.part + (long)tn * kParts + part_of(rank, tid, jj)] = v;
                     }
                 }
                 finish_step(z, nb, t >= 0, lmin, tn - 1, slot_ws);
