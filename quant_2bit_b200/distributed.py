@@ -190,7 +190,7 @@ class GatherHandle:
     def __init__(self, gathered, side, pads):
         self.gathered = gathered
         self._side = side
-        self._pads = pads     # (i, buffer, B, per) of ragged gathers to compact
+        self._pads = pads     # (i, buffer, B, world, per) of ragged gathers to compact
 
     def wait(self):
         if self._side is not None:
