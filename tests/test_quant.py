@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN
+from conftest import GOLDEN, ROOT
 from oracle import torch_port
 
 
@@ -37,9 +37,10 @@ def test_tile_order_matches_reference_and_round_trips():
 
 
 def test_hook_patches_reference_modules():
-    ref = os.environ.get("QUANT2BIT_REFERENCE", "/root/reference")
+    # the reference's own package, installed unmodified in baseline/_ref
+    ref = os.environ.get("QUANT2BIT_REFERENCE", os.path.join(ROOT, "baseline", "_ref"))
     if not os.path.isdir(os.path.join(ref, "src", "bcjr")):
-        pytest.skip("reference checkout not present")
+        pytest.skip("reference install not present")
     sys.path.insert(0, ref)
     try:
         import src.bcjr.bcjr_quant as bq
