@@ -5,6 +5,7 @@
 The library is a plain C-ABI shared object (include/bcjr_b200.h); it links
 the CUDA runtime statically and has no torch dependency.
 """
+import concurrent.futures
 import os
 import subprocess
 import sys
@@ -39,8 +40,8 @@ def build(force=False, verbose=False, ptxas_info=False):
     """Compile every source into one shared library (skipped when up to date)."""
     if not force and not _stale():
         return LIB
-    objs = []
     srcs = [s for s in SOURCES if os.path.exists(os.path.join(CSRC, s))]
+    cmds, objs = [], []
     for s in srcs:
         obj = os.path.join(CSRC, s.replace(".cu", ".o"))
         cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, "-c", os.path.join(CSRC, s), "-o", obj]
@@ -48,8 +49,12 @@ def build(force=False, verbose=False, ptxas_info=False):
             cmd += ["-Xptxas", "-v"]
         if verbose:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
         objs.append(obj)
+    # the translation units are independent: compile them side by side
+    with concurrent.futures.ThreadPoolExecutor(max_workers=min(len(cmds), os.cpu_count() or 1)) as ex:
+        for f in [ex.submit(subprocess.run, c, check=True) for c in cmds]:
+            f.result()
     cmd = [_nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", *objs, "-o", LIB]
     if verbose:
         print(" ".join(cmd), flush=True)
