@@ -398,7 +398,8 @@ def run_layer(args, rank, world, local_rank):
     value = seqs_total * edges_per_seq * args.steps / (t_step / 1e3)
     sms = props.multi_processor_count
     clk_mhz = clk.get("sm_max_mhz") or 1965.0
-    peak = sms * MUFU_PER_SM_CLK * clk_mhz * 1e6 / 1e9
+    from quant_2bit_b200 import _lib
+    peak = _lib.measure_mufu_gops(dev)          # measured ex2 throughput of this GPU
     mufu_ops = sum(MUFU[V]) * seqs_total * NSTEP * (1 << L) / world
     bcjr_ms = (t_step - t_wrap) / args.steps
     elems = sum(W.numel() for W, _, _, _ in mats)
@@ -720,7 +721,9 @@ def run_bcjr(args, rank, world, local_rank):
                         else ("forward", fwd_avg, MUFU_FWD * sstep))
     sms = props.multi_processor_count
     clk_mhz = clk.get("sm_max_mhz") or 1965.0
-    peak = sms * MUFU_PER_SM_CLK * clk_mhz * 1e6 / 1e9          # Gop/s at max SM clock
+    spec_peak = sms * MUFU_PER_SM_CLK * clk_mhz * 1e6 / 1e9     # Gop/s at max SM clock
+    # measured MUFU throughput of this GPU (ex2 probe kernel), the roofline's denominator
+    peak = _lib.measure_mufu_gops(dev)
     achieved = ops / (dom_ms / 1e3) / 1e9
     fma = FMA_CYCLES_PER_STATE_STEP[V][dom]
     fp32 = None
@@ -766,12 +769,14 @@ def run_bcjr(args, rank, world, local_rank):
             "kernel_ms": {"forward": fwd_avg, "backward": bwd_avg},
             "roofline": {"bound": "mufu", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "Gop/s", "frac": achieved / peak,
+                         "peak_kind": "measured: best of 3 launches of bcjr_probe_mufu (ex2.approx "
+                                      "throughput, 8 chains x 1024 threads per SM) on this GPU",
+                         "spec_peak": spec_peak, "frac_of_spec": achieved / spec_peak,
                          "traffic": DRAM_BYTES_PER_SEQ[V][dom] * Bl,
                          "traffic_unit": "bytes per launch (ncu capture of a small launch "
                                          "scaled by sequences; see profiles/)",
                          "note": f"algorithmic MUFU ops: {MUFU_FWD}/{MUFU_BWD} per state-step "
-                                 f"(fwd/bwd call), peak = {sms} SMs x 16/clk x {clk_mhz:.0f} MHz "
-                                 "(derived; not in MEASURED_PEAKS.json)"},
+                                 f"(fwd/bwd call); spec_peak = {sms} SMs x 16/clk x {clk_mhz:.0f} MHz"},
             "fp32_issue": fp32,
             "e2e": {"value": e2e_value, "unit": UNIT, "steps": e2e_steps,
                     "h2d_bytes_per_step": w_host.numel() * 4,

@@ -195,6 +195,17 @@ BCJR_API int bcjr_fb_forward_noalloc(const float *seq, const float *cb, const fl
                                      float *soft, float *logZ, bcjr_stream_t stream);
 
 /*
+ * MUFU throughput probe, a diagnostic: launches 4 x (SM count) blocks of 256
+ * threads, each thread running 8 independent chains of `iters`
+ * ex2.approx.f32 operations, and writes the number of ex2 operations launched
+ * to *ops (host pointer).  Timed with events on `stream`, ops / time is the
+ * MUFU pipe's measured throughput: the roofline denominator of the BCJR
+ * kernels, which are bound by that pipe.  `out` is one device float that
+ * the kernel never writes in practice.  No counterpart in the reference.
+ */
+BCJR_API int bcjr_probe_mufu(float *out, int iters, double *ops, bcjr_stream_t stream);
+
+/*
  * Randomized Hadamard transform and tiling around the op: the caller side
  * of the reference's quantizer wrapper.  m, n are powers of two in
  * [16, 32768]; fp32 matrices row-major; sign vectors of +-1 (length m for

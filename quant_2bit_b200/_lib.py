@@ -53,6 +53,7 @@ SIGNATURES = {
     "bcjr_viterbi_workspace_bytes": ([_I, _I, _I, _I, _I], _SZ),
     "bcjr_viterbi": ([_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _SZ, _P], _I),
     "bcjr_hyb_codebook": ([_P, _I, _I, _P, _P], _I),
+    "bcjr_probe_mufu": ([_P, _I, ctypes.POINTER(ctypes.c_double), _P], _I),
 }
 
 _lib = None
@@ -144,3 +145,24 @@ def workspace(B, N, L, k, V, flags, device):
     if n == 0:
         check(lib.bcjr_check_shape(B, N, L, k, V) or BCJR_ERR_UNSUPPORTED, "bcjr_workspace_bytes")
     return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def measure_mufu_gops(device, iters=8192, repeats=3):
+    """Measured MUFU (ex2) throughput of this GPU in Gop/s: the best of
+    `repeats` timed launches of bcjr_probe_mufu on the current stream."""
+    lib = load()
+    out = torch.zeros(1, dtype=torch.float32, device=device)
+    ops = ctypes.c_double(0.0)
+    stream = torch.cuda.current_stream(device)
+    best = None
+    for r in range(repeats + 1):          # the first launch warms up
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        check(lib.bcjr_probe_mufu(ptr(out), int(iters), ctypes.byref(ops),
+                                  ctypes.c_void_p(stream.cuda_stream)), "bcjr_probe_mufu")
+        e1.record(stream)
+        e1.synchronize()
+        if r:
+            g = ops.value / (e0.elapsed_time(e1) / 1e3) / 1e9
+            best = g if best is None else max(best, g)
+    return best

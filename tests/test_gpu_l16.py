@@ -272,3 +272,22 @@ def test_reserved_sms_leave_results_unchanged(cuda_ok, V, N, B):
     for o in outs[1:]:
         for a, b in zip(o, outs[0]):
             assert torch.equal(a, b)
+
+
+def test_mufu_probe_measures_the_pipe(cuda_ok):
+    """bcjr_probe_mufu, the measured roofline denominator: its ex2 rate lies
+    between 60 % and 105 % of 148 SMs x 16 ops per clock at the B200's
+    1965 MHz maximum (4653 Gop/s), and its op count is what was launched."""
+    import ctypes
+    from quant_2bit_b200 import _lib
+    dev = torch.device("cuda")
+    gops = _lib.measure_mufu_gops(dev, iters=4096, repeats=2)
+    spec = torch.cuda.get_device_properties(dev).multi_processor_count * 16 * 1.965
+    assert 0.6 * spec < gops < 1.05 * spec, (gops, spec)
+    lib = _lib.load()
+    ops = ctypes.c_double(0.0)
+    out = torch.zeros(1, device=dev)
+    assert lib.bcjr_probe_mufu(_lib.ptr(out), 10, ctypes.byref(ops), _lib.stream_ptr(dev)) == 0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    assert ops.value == sms * 4 * 256 * 10 * 8
+    assert lib.bcjr_probe_mufu(_lib.ptr(out), 0, ctypes.byref(ops), _lib.stream_ptr(dev)) == 1
