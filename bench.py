@@ -1,7 +1,7 @@
 """Benchmark: BCJR forward+backward state-transitions/sec on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c5|v2|layer|viterbi] [--temperature T] [--weights gauss|t3]
+                    [--config c2|c3|c5|v2|layer|viterbi|viterbi1] [--temperature T] [--weights gauss|t3]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU, NCCL)
 
 Workload (synthetic, seeded): L=16, k=2, V=1, N=256 steps, T=0.5, codebook
@@ -28,6 +28,8 @@ randn(65536) (seed 0), weights randn drawn after the codebook.
 * viterbi: hard (min-sum) Viterbi encoding of config v2's sequences (one
   1024x1024 weight per GPU at L=16, k=2, V=2), the reference's
   viterbi_encode_v_batched_cuda; its own metric (min-sum transitions/s).
+* viterbi1: the same at V=1 (config c2's 4096 sequences of N=256), the
+  reference's viterbi_encode (src/viterbi/encode.py:47-90).
 
 One step = forward (soft) + backward (d_seq for an upstream gradient of ones)
 of every local sequence (+ the per-weight all-gathers when N > 1; the
@@ -63,8 +65,12 @@ UNIT = "transitions/s"
 L, K_BITS, TEMP = 16, 2, 0.5
 # (V, N) per config
 SHAPES = {"c2": (1, 256), "c3": (1, 256), "c5": (1, 256), "v2": (2, 128), "layer": (2, 128),
-          "viterbi": (2, 128)}
-VITERBI_METRIC = "Viterbi (min-sum) state-transitions/sec (L=16,k=2,V=2), 1 B200"
+          "viterbi": (2, 128), "viterbi1": (1, 256)}
+VITERBI_CONFIGS = ("viterbi", "viterbi1")
+
+
+def viterbi_metric(V):
+    return f"Viterbi (min-sum) state-transitions/sec (L=16,k=2,V={V}), 1 B200"
 # Algorithmic MUFU (ex2/lg2/rcp) per state-step, forward call and backward
 # call: alpha LSE (2^b+1)/2^b + beta LSE (2^b+1)/2^b + marginal exp 1 for the
 # forward; the same recompute plus 2/2^b softmax normalisers for the
@@ -143,7 +149,7 @@ def make_inputs(config, rank, world, weights="gauss"):
     V, NSTEP = SHAPES[config]
     g = torch.Generator().manual_seed(0)
     cb = torch.randn(1 << L, V, generator=g)
-    if config in ("c2", "v2", "viterbi"):
+    if config in ("c2", "v2") + VITERBI_CONFIGS:
         gw = torch.Generator().manual_seed(1000 + rank) if rank else g
         w = torch.randn(4096, NSTEP, V, generator=gw)
         if weights == "t3":
@@ -270,7 +276,7 @@ def cpu_reference(args, nseq, steps, warmup):
     src/bcjr/bcjr_quant.py:60): `warmup` untimed steps, then `steps` timed
     steps, each one forward + backward (upstream gradient of ones) of the
     same `nseq`-sequence sample of the workload."""
-    if args.config == "viterbi":
+    if args.config in VITERBI_CONFIGS:
         return cpu_viterbi(args)
     V, NSTEP = SHAPES[args.config]
     edges_per_seq = NSTEP * (1 << L) * (1 << (K_BITS * V))
@@ -435,41 +441,67 @@ def run_layer(args, rank, world, local_rank):
     print(json.dumps(result), flush=True)
 
 
-def cpu_viterbi(args):
-    """The reference's exact-arithmetic Viterbi encoder (viterbi_encode_v,
-    restated vectorised in oracle/viterbi.py) on the host cores, on a bounded
-    sample of config viterbi's sequences."""
+def viterbi_reference():
+    """(fn(seqs (B, N V) float32, cb (2^L, V), V) -> None, kind): the
+    reference's fastest host encoder, viterbi_encode_v_batched
+    (src/viterbi/encode.py:425-470: numpy, local costs by a BLAS matmul),
+    imported unmodified from its install in baseline/_ref; without that
+    install, the exact-arithmetic restatement oracle/viterbi.py."""
+    if os.path.isdir(os.path.join(REF_DIR, "src", "viterbi")):
+        sys.path.insert(0, REF_DIR)
+        try:
+            from src.viterbi.encode import viterbi_encode_v_batched as ref
+        finally:
+            sys.path.remove(REF_DIR)
+
+        def run(seqs, cb, V):
+            ref(seqs, L, K_BITS, V, lambda st: cb[st])
+        return run, "reference"
     from oracle import viterbi as ov
-    V, NSTEP = SHAPES["viterbi"]
-    cb, w, _ = make_inputs("viterbi", 0, 1)
+
+    def run(seqs, cb, V):
+        ov.viterbi(seqs, cb, L, K_BITS, V)
+    return run, "port"
+
+
+def cpu_viterbi(args):
+    """The reference's host Viterbi encoder (viterbi_reference) on a bounded
+    sample of the Viterbi config's sequences, on the host cores."""
+    V, NSTEP = SHAPES[args.config]
+    cb, w, _ = make_inputs(args.config, 0, 1)
     nseq = max(args.cpu_sample_seqs, 4)
     sample = w[:nseq].reshape(nseq, NSTEP * V).numpy()
     cbn = cb.numpy()
-    for _ in range(args.warmup if args.impl == "reference" else 0):
-        ov.viterbi(sample, cbn, L, K_BITS, V)
+    run, kind = viterbi_reference()
+    for _ in range(args.warmup if args.impl == "reference" else 1):
+        run(sample, cbn, V)
     steps = args.steps if args.impl == "reference" else 1
     t0 = time.perf_counter()
     for _ in range(steps):
-        ov.viterbi(sample, cbn, L, K_BITS, V)
+        run(sample, cbn, V)
     dt = (time.perf_counter() - t0) / steps
     value = nseq * NSTEP * (1 << L) * (1 << (K_BITS * V)) / dt
-    return {"value": value, "unit": UNIT, "cores": 1, "kind": "port", "sample_sequences": nseq,
-            "sample": f"{nseq} sequences of config viterbi (L=16, V=2, N=128), numpy "
-                      f"{np.__version__} (one thread of vector work), {dt:.2f} s per step"}
+    what = ("viterbi_encode_v_batched, unmodified (numpy " + np.__version__ +
+            ", BLAS matmul threads up to all host cores)" if kind == "reference"
+            else "oracle/viterbi.py (numpy " + np.__version__ + ", one thread)")
+    return {"value": value, "unit": UNIT, "cores": (os.cpu_count() or 1) if kind == "reference" else 1,
+            "kind": kind, "sample_sequences": nseq, "cpu_model": cpu_model(),
+            "sample": f"{nseq} sequences of config {args.config} (L=16, V={V}, N={NSTEP}), "
+                      f"{what}, {dt:.2f} s per step"}
 
 
 def run_viterbi(args, rank, world, local_rank):
-    """--config viterbi: one 1024x1024 weight per GPU as 4096 sequences of 128
-    two-dimensional steps, hard Viterbi encoded (bitstreams, start states,
-    reconstructions, MSEs)."""
+    """--config viterbi / viterbi1: one 1024x1024 weight per GPU as 4096
+    sequences of 128 two-dimensional steps (V=2) or 256 scalar steps (V=1),
+    hard Viterbi encoded (bitstreams, start states, reconstructions, MSEs)."""
     from quant_2bit_b200.viterbi import viterbi_encode_batched
-    V, NSTEP = SHAPES["viterbi"]
+    V, NSTEP = SHAPES[args.config]
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
-    cb_cpu, w_cpu, _ = make_inputs("viterbi", rank, world)
+    cb_cpu, w_cpu, _ = make_inputs(args.config, rank, world)
     if args.sequences:
         w_cpu = w_cpu[:args.sequences]
     Bl = w_cpu.shape[0]
@@ -522,31 +554,33 @@ def run_viterbi(args, rank, world, local_rank):
     per_seq = NSTEP * (1 << L) * (1 << (K_BITS * V))
     value = Bl * world * per_seq * args.steps / (t_ms / 1e3)
     # issue roofline: per state-step the exact min-sum needs d = c - w and its
-    # square for 2 dimensions, their sum, the add of the group minimum (3 f32x2
-    # instructions per 2 states = 3 per state) and a compare / select for the
-    # minimum and its index (2 per state): 5 thread instructions; peak 128
-    # thread instructions per clock per SM
+    # square per dimension, their sum at V=2, the add of the group minimum
+    # (f32x2 instructions: 3 per state at V=2, 1.5 at V=1) and a compare /
+    # select for the minimum and its index (2 per state): 5 (V=2) or 3.5
+    # (V=1) thread instructions; peak 128 thread instructions per clock per SM
     sms = props.multi_processor_count
     clk_mhz = clk.get("sm_max_mhz") or 1965.0
-    ops = 5.0 * Bl * NSTEP * (1 << L) * args.steps
+    inst = 5.0 if V == 2 else 3.5
+    ops = inst * Bl * NSTEP * (1 << L) * args.steps
     achieved = ops / (t_ms / 1e3) / 1e9
     peak = sms * 128 * clk_mhz * 1e6 / 1e9
     result = {
-        "metric": VITERBI_METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "metric": viterbi_metric(V), "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded randn codebook (65536, 2) and weights)",
-        "config": {"workload": "viterbi: one 1024x1024 weight per GPU, 4096 sequences of "
-                               "N=128 at L=16, k=2, V=2 (bitstreams, starts, recons, MSEs)",
+        "data": f"synthetic (seeded randn codebook (65536, {V}) and weights)",
+        "config": {"workload": f"{args.config}: one 1024x1024 weight per GPU, {Bl} sequences of "
+                               f"N={NSTEP} at L=16, k=2, V={V} (bitstreams, starts, recons, MSEs)",
                    "sequences_per_gpu": Bl, "sequences_total": Bl * world,
                    "l2": "flushed between timed steps (256 MB write, outside the events)"},
         "clocks": clk,
         "gpu_launches": 2 * args.steps,
-        "roofline": {"bound": "issue", "kernel": "vit_b4_kernel + walk-back",
+        "roofline": {"bound": "issue",
+                     "kernel": f"vit_b{2 * V}_kernel + walk-back",
                      "achieved": achieved, "peak": peak, "unit": "Ginst/s", "frac": achieved / peak,
-                     "traffic": float(Bl * NSTEP * 4096),
+                     "traffic": float(Bl * NSTEP * 4096),   # one byte per 4 (V=1) or 16 groups
                      "traffic_unit": "backpointer bytes written per launch",
-                     "note": "5 algorithmic thread instructions per state-step; "
+                     "note": f"{inst:g} algorithmic thread instructions per state-step; "
                              f"peak {sms} SMs x 128/clk x {clk_mhz:.0f} MHz"},
         "e2e": {"value": Bl * world * per_seq * args.steps / (t_e2e / 1e3), "unit": UNIT,
                 "h2d_bytes_per_step": host_in.numel() * 4,
@@ -811,7 +845,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c3", choices=["c2", "c3", "c5", "v2", "layer", "viterbi"])
+    ap.add_argument("--config", default="c3",
+                    choices=["c2", "c3", "c5", "v2", "layer", "viterbi", "viterbi1"])
     ap.add_argument("--temperature", type=float, default=TEMP,
                     help="T (config 4 sweeps 4, 2, 1, 0.5, 0.25, 0.1, 0.05)")
     ap.add_argument("--weights", default="gauss", choices=["gauss", "t3"],
@@ -841,17 +876,18 @@ def main():
         nsample = args.ref_sample_seqs
         ref = cpu_reference(args, nsample, args.steps, args.warmup)
         nsample = ref.get("sample_sequences", nsample)
-        line = {"metric": VITERBI_METRIC if args.config == "viterbi" else METRIC,
+        line = {"metric": viterbi_metric(V) if args.config in VITERBI_CONFIGS else METRIC,
                 "value": ref["value"], "unit": UNIT, "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": nsample * EDGES_PER_SEQ / ref["value"] * 1e3,
                 "higher_is_better": True,
-                "scaling": "weak" if args.config in ("c2", "v2", "viterbi") else "strong",
+                "scaling": "weak" if args.config in ("c2", "v2") + VITERBI_CONFIGS else "strong",
                 "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic (seeded randn codebook and weights of the workload's shapes)",
                 "impl": "reference",
-                "config": {"workload": f"{args.config}: L=16 k=2 V={V} N={NSTEP} T={args.temperature:g} "
-                                       f"{args.weights} weights, CPU sample of {nsample} sequence(s) per step",
+                "config": {"workload": f"{args.config}: L=16 k=2 V={V} N={NSTEP} "
+                                       + ("" if args.config in VITERBI_CONFIGS else f"T={args.temperature:g} ")
+                                       + f"{args.weights} weights, CPU sample of {nsample} sequence(s) per step",
                            "sample_sequences": nsample},
                 "cpu_baseline": ref,
                 "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -861,7 +897,7 @@ def main():
 
     if args.config == "layer":
         run_layer(args, rank, world, local_rank)
-    elif args.config == "viterbi":
+    elif args.config in VITERBI_CONFIGS:
         run_viterbi(args, rank, world, local_rank)
     else:
         run_bcjr(args, rank, world, local_rank)

@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libbcjr_b200.so")
 SOURCES = ["bcjr_capi.cu", "bcjr_generic.cu", "bcjr_l16.cu", "bcjr_b4.cu", "bcjr_noalloc.cu", "bcjr_rht.cu",
-           "bcjr_viterbi.cu", "bcjr_vit_b4.cu", "bcjr_codes.cu", "bcjr_l16_cl4.cu", "bcjr_probe.cu"]
+           "bcjr_viterbi.cu", "bcjr_vit_b4.cu", "bcjr_vit_b2.cu", "bcjr_codes.cu", "bcjr_l16_cl4.cu", "bcjr_probe.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-fvisibility=hidden"]

@@ -159,6 +159,9 @@ vit_b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
                     if (tid == 0 && !failed) mbar_arm(bar, kBytes);
                     wait_bar(bar, (use[z] >> 1) & 1, status, failed);
+                    // lanes give up independently: the warp sends (and
+                    // syncs) only if none of them has
+                    failed = __any_sync(0xffffffffu, failed);
                     in = sm.buf[z][x];
                     ++use[z];
                 }
@@ -248,8 +251,10 @@ vit_b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
                 final_states[sidx[z]] = (i >= 0 && i < (1 << kL)) ? i : 0;
             }
         }
+        // rank 0 has read cv / ci before any CTA writes the next group's
+        // (with N = 1 nothing else orders the two)
+        cluster_sync();
     }
-    cluster_sync();
 }
 
 // Walk back, one thread per sequence: state at t-1 = (bp_t(s >> 4) << 12) | (s >> 4).

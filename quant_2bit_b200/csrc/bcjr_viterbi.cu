@@ -197,12 +197,21 @@ extern "C" {
 
 // Workspace: a 256-byte header (device status word, read by bcjr_ws_status)
 // then the kernel's data: the cluster kernel's backpointers for L=16, k=2,
-// V=2 (bcjr_vit_b4.cu), else sequence slots of the generic kernel.
+// V=2 (bcjr_vit_b4.cu) or L=16, k=2, V=1 (bcjr_vit_b2.cu), else sequence
+// slots of the generic kernel.
 constexpr size_t kVitHeader = 256;
 
-bool vit_use_cluster(int N, int L, int k, int V, const void *cb) {
-    if (bcjr::test_option(bcjr::kOptForceGeneric)) return false;
-    return bcjr::vit_b4_applicable(N, L, k, V, cb);
+// The cluster kernel for this shape: 4 (b = 4), 2 (b = 2) or 0 (none).
+int vit_cluster(int N, int L, int k, int V, const void *cb) {
+    if (bcjr::test_option(bcjr::kOptForceGeneric)) return 0;
+    if (bcjr::vit_b4_applicable(N, L, k, V, cb)) return 4;
+    if (bcjr::vit_b2_applicable(N, L, k, V, cb)) return 2;
+    return 0;
+}
+
+size_t vit_cluster_bytes(int which, int B, int N) {
+    return which == 4 ? bcjr::vit_b4_workspace_bytes(B, N)
+                      : which == 2 ? bcjr::vit_b2_workspace_bytes(B, N) : 0;
 }
 
 BCJR_API size_t bcjr_viterbi_workspace_bytes(int B, int N, int L, int k, int V) {
@@ -211,8 +220,9 @@ BCJR_API size_t bcjr_viterbi_workspace_bytes(int B, int N, int L, int k, int V) 
     if (cap <= 0) return 0;
     const long grid = B < cap ? (B > 0 ? B : 1) : cap;
     size_t need = (size_t)grid * bcjr::vit::slot_bytes(N, L, k * V);
-    if (vit_use_cluster(N, L, k, V, nullptr)) {
-        const size_t c = bcjr::vit_b4_workspace_bytes(B, N);
+    const int which = vit_cluster(N, L, k, V, nullptr);
+    if (which) {
+        const size_t c = vit_cluster_bytes(which, B, N);
         if (c > need) need = c;
     }
     return kVitHeader + need;
@@ -242,12 +252,16 @@ BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L
     void *data = static_cast<char *>(ws) + kVitHeader;
     const size_t data_bytes = ws_bytes - kVitHeader;
     if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return BCJR_ERR_LAUNCH;
-    if (vit_use_cluster(N, L, k, V, cb) && data_bytes >= bcjr::vit_b4_workspace_bytes(B, N)) {
+    const int which = vit_cluster(N, L, k, V, cb);
+    if (which && data_bytes >= vit_cluster_bytes(which, B, N)) {
         // Test-only (BCJR_OPT_TEST_DROP_SENDS): the cluster kernel's CTA 1
         // withholds its outputs so that the bounded waits time out.
-        const cudaError_t e = bcjr::launch_vit_b4(seq, cb, B, N, bitstreams, start_states, recons,
-                                                  mses, data, data_bytes, status,
-                                                  bcjr::test_option(bcjr::kOptDropSends) ? 1 : 0, s);
+        const int drop = bcjr::test_option(bcjr::kOptDropSends) ? 1 : 0;
+        const cudaError_t e =
+            which == 4 ? bcjr::launch_vit_b4(seq, cb, B, N, bitstreams, start_states, recons, mses,
+                                             data, data_bytes, status, drop, s)
+                       : bcjr::launch_vit_b2(seq, cb, B, N, bitstreams, start_states, recons, mses,
+                                             data, data_bytes, status, drop, s);
         return e == cudaSuccess ? BCJR_OK : BCJR_ERR_LAUNCH;
     }
     const size_t slot = bcjr::vit::slot_bytes(N, L, k * V);

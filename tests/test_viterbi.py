@@ -60,16 +60,24 @@ def test_kernel_matches_reference_encoder(cuda_ok, name):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("L,k,V,B,N,kind", [(16, 2, 2, 301, 128, "hyb"), (16, 2, 1, 5, 256, "gauss"),
+                                            (16, 2, 1, 150, 32, "gauss"), (16, 2, 1, 600, 1, "gauss"),
+                                            (16, 2, 2, 600, 1, "gauss"), (16, 2, 1, 3, 512, "tied"),
                                             (16, 2, 2, 2, 1, "gauss"), (12, 1, 2, 7, 33, "gauss"),
                                             (4, 2, 2, 3, 9, "gauss"), (16, 4, 1, 2, 64, "gauss")])
 def test_kernel_matches_oracle(cuda_ok, L, k, V, B, N, kind):
-    """Ragged and large batches (more sequences than blocks), N = 1, the
-    smallest trellis, and a HYB codebook (repeated codewords: exact ties,
-    resolved to the lowest index as in the reference)."""
+    """Ragged and large batches (more sequences than blocks or cluster
+    slots), N = 1 with several sequence groups per cluster, the smallest
+    trellis, and codebooks with repeated codewords (HYB; "tied": 64 distinct
+    values) whose exact ties resolve to the lowest index as in the
+    reference."""
     from quant_2bit_b200.viterbi import viterbi_encode_batched
     rng = np.random.default_rng(L * 100 + B)
-    cb = (hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32)) if kind == "hyb"
-          else rng.standard_normal((1 << L, V)).astype(np.float32))
+    if kind == "hyb":
+        cb = hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32))
+    elif kind == "tied":
+        cb = rng.standard_normal(64).astype(np.float32)[rng.integers(0, 64, (1 << L, V))]
+    else:
+        cb = rng.standard_normal((1 << L, V)).astype(np.float32)
     seqs = rng.standard_normal((B, N * V)).astype(np.float32)
     out = viterbi_encode_batched(torch.tensor(seqs, device="cuda"), torch.tensor(cb, device="cuda"),
                                  L, k, V)
@@ -96,27 +104,33 @@ def test_reference_entry_point_and_errors(cuda_ok):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("B,N", [(64, 128), (2049, 8), (3, 512)])
-def test_cluster_and_generic_kernels_agree(cuda_ok, B, N):
-    """L=16, k=2, V=2 runs on the 4-CTA cluster kernel; the test option
-    BCJR_OPT_FORCE_GENERIC sends it to the one-block-per-sequence kernel.
-    Both are exact: identical results, across the 2048-sequence chunking of
-    the cluster path and at the longest N it serves."""
+@pytest.mark.parametrize("V,B,N", [(2, 64, 128), (2, 2049, 8), (2, 3, 512),
+                                   (1, 64, 256), (1, 1000, 8), (1, 449, 512)])
+def test_cluster_and_generic_kernels_agree(cuda_ok, V, B, N):
+    """L=16, k=2 runs on the 4-CTA cluster kernels (b = 4 at V=2, b = 2 at
+    V=1); the test option BCJR_OPT_FORCE_GENERIC sends it to the
+    one-block-per-sequence kernel.  Both are exact: identical results,
+    across the chunking of the cluster paths (2048 sequences at V=2, whole
+    waves of at most 2^18 / N sequences at V=1: 449 x 512 takes two
+    chunks) and at the longest N they serve."""
     from quant_2bit_b200 import _lib
     from quant_2bit_b200.viterbi import viterbi_encode_batched
-    rng = np.random.default_rng(B + N)
-    cb = torch.tensor(hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32)), device="cuda")
-    seqs = torch.tensor(rng.standard_normal((B, 2 * N)).astype(np.float32), device="cuda")
-    a = viterbi_encode_batched(seqs, cb, 16, 2, 2)
+    rng = np.random.default_rng(B + N + V)
+    cb = (hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32)) if V == 2
+          else rng.standard_normal((1 << 16, 1)).astype(np.float32))
+    cb = torch.tensor(cb, device="cuda")
+    seqs = torch.tensor(rng.standard_normal((B, V * N)).astype(np.float32), device="cuda")
+    a = viterbi_encode_batched(seqs, cb, 16, 2, V)
     with _lib.test_option(_lib.OPT_FORCE_GENERIC, 1):
-        b = viterbi_encode_batched(seqs, cb, 16, 2, 2)
+        b = viterbi_encode_batched(seqs, cb, 16, 2, V)
     for x, y in zip(a[:3], b[:3]):
         assert torch.equal(x, y)
     torch.testing.assert_close(a[3], b[3], rtol=1e-6, atol=1e-7)
 
 
 @pytest.mark.gpu
-def test_cluster_wait_timeout_is_reported_and_context_survives(cuda_ok):
+@pytest.mark.parametrize("V", [2, 1])
+def test_cluster_wait_timeout_is_reported_and_context_survives(cuda_ok, V):
     """Failure detection without a GPU fault: with the test option
     BCJR_OPT_TEST_DROP_SENDS one CTA of each cluster withholds its group
     minima, every bounded wait of the cluster Viterbi expires (~1 s), the
@@ -129,22 +143,24 @@ def test_cluster_wait_timeout_is_reported_and_context_survives(cuda_ok):
     dev = torch.device("cuda")
     rng = np.random.default_rng(17)
     B, N = 8, 16
-    cb = torch.tensor(hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32)), device=dev)
-    seqs = torch.tensor(rng.standard_normal((B, 2 * N)).astype(np.float32), device=dev)
+    cb = (hyb_codebook(rng.standard_normal((512, 2)).astype(np.float32)) if V == 2
+          else rng.standard_normal((1 << 16, 1)).astype(np.float32))
+    cb = torch.tensor(cb, device=dev)
+    seqs = torch.tensor(rng.standard_normal((B, V * N)).astype(np.float32), device=dev)
     bits = torch.empty((B, N), dtype=torch.int32, device=dev)
     starts = torch.empty((B,), dtype=torch.int32, device=dev)
-    rec = torch.empty((B, 2 * N), dtype=torch.float32, device=dev)
+    rec = torch.empty((B, V * N), dtype=torch.float32, device=dev)
     mse = torch.empty((B,), dtype=torch.float32, device=dev)
-    ws = torch.empty(lib.bcjr_viterbi_workspace_bytes(B, N, 16, 2, 2), dtype=torch.uint8, device=dev)
+    ws = torch.empty(lib.bcjr_viterbi_workspace_bytes(B, N, 16, 2, V), dtype=torch.uint8, device=dev)
     P, sp = _lib.ptr, _lib.stream_ptr(dev)
     with _lib.test_option(_lib.OPT_TEST_DROP_SENDS, 1):
-        rc = lib.bcjr_viterbi(P(seqs), P(cb), B, N, 16, 2, 2, P(bits), P(starts), P(rec), P(mse),
+        rc = lib.bcjr_viterbi(P(seqs), P(cb), B, N, 16, 2, V, P(bits), P(starts), P(rec), P(mse),
                               P(ws), ws.numel(), sp)
     assert rc == 0
     assert lib.bcjr_ws_status(P(ws), sp) == _lib.BCJR_ERR_TIMEOUT
-    assert int(starts.max()) < 65536 and int(bits.max()) < 16
+    assert int(starts.max()) < 65536 and int(bits.max()) < (1 << (2 * V))
     assert torch.isnan(rec).all() and torch.isnan(mse).all()
-    out = [o.cpu().numpy() for o in viterbi_encode_batched(seqs, cb, 16, 2, 2)]
-    ref = viterbi.viterbi(seqs.cpu().numpy(), cb.cpu().numpy(), 16, 2, 2)
+    out = [o.cpu().numpy() for o in viterbi_encode_batched(seqs, cb, 16, 2, V)]
+    ref = viterbi.viterbi(seqs.cpu().numpy(), cb.cpu().numpy(), 16, 2, V)
     for a, b in zip(out[:3], ref[:3]):
         np.testing.assert_array_equal(a, b)
