@@ -262,12 +262,19 @@ BCJR_API int bcjr_untile_irht(const float *seqs, const float *sign_l, const floa
  * multiply-add), ties go to the lowest predecessor index and the lowest
  * final state, so walks are bit-identical to it.  Shapes as for the BCJR
  * op; workspace of bcjr_viterbi_workspace_bytes bytes, 256-byte aligned
- * (L=16, k=2, V=2 runs on 4-CTA clusters and needs N * 4096 bytes per
- * sequence for up to 2048 sequences at a time; other shapes run fewer
- * sequences at a time when given fewer bytes).  bcjr_ws_status reports a
- * device-side wait timeout.
+ * (L=16, k=2 runs on 4-CTA clusters for N <= 512 and needs N * 4096 bytes
+ * per sequence, for up to 2048 sequences at a time at V=2 and up to
+ * 2^18 / N at V=1; other shapes run fewer sequences at a time when given
+ * fewer bytes).  bcjr_ws_status reports a device-side wait timeout.
+ * bcjr_viterbi_launches: the number of kernels one bcjr_viterbi call with
+ * these shapes launches on the current device given a workspace of
+ * bcjr_viterbi_workspace_bytes (one per chunk of sequences and its
+ * walk-back on the cluster paths, one otherwise; 0 for B = 0, a negative
+ * error code for an unsupported shape).  No counterpart in the reference:
+ * launch accounting for benchmarks.
  */
 BCJR_API size_t bcjr_viterbi_workspace_bytes(int B, int N, int L, int k, int V);
+BCJR_API int bcjr_viterbi_launches(int B, int N, int L, int k, int V);
 BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L, int k, int V,
                           int *bitstreams, int *start_states, float *recons, float *mses,
                           void *ws, size_t ws_bytes, bcjr_stream_t stream);

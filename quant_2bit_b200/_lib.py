@@ -51,6 +51,7 @@ SIGNATURES = {
     "bcjr_rht_tile": ([_P, _P, _P, _I, _I, _P, _P, _P, _P, _SZ, _P], _I),
     "bcjr_untile_irht": ([_P, _P, _P, _I, _I, _P, _P, _P, _SZ, _P], _I),
     "bcjr_viterbi_workspace_bytes": ([_I, _I, _I, _I, _I], _SZ),
+    "bcjr_viterbi_launches": ([_I, _I, _I, _I, _I], _I),
     "bcjr_viterbi": ([_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _SZ, _P], _I),
     "bcjr_hyb_codebook": ([_P, _I, _I, _P, _P], _I),
     "bcjr_probe_mufu": ([_P, _I, ctypes.POINTER(ctypes.c_double), _P], _I),

@@ -76,6 +76,7 @@ cudaError_t launch_b4(const LaunchArgs &a);
 // Cluster Viterbi for L=16, k=2, V=2, 1 <= N <= 512 (bcjr_vit_b4.cu).
 bool vit_b4_applicable(int N, int L, int k, int V, const void *cb);
 size_t vit_b4_workspace_bytes(int B, int N);
+int vit_b4_launches(int B);
 cudaError_t launch_vit_b4(const float *seq, const float *cb, int B, int N, int *bits,
                           int *starts, float *recon, float *mse, void *ws, size_t ws_bytes,
                           int *status, int drop_sends, cudaStream_t st);
@@ -83,6 +84,7 @@ cudaError_t launch_vit_b4(const float *seq, const float *cb, int B, int N, int *
 // Cluster Viterbi for L=16, k=2, V=1, 1 <= N <= 512 (bcjr_vit_b2.cu).
 bool vit_b2_applicable(int N, int L, int k, int V, const void *cb);
 size_t vit_b2_workspace_bytes(int B, int N);
+int vit_b2_launches(int B, int N);
 cudaError_t launch_vit_b2(const float *seq, const float *cb, int B, int N, int *bits,
                           int *starts, float *recon, float *mse, void *ws, size_t ws_bytes,
                           int *status, int drop_sends, cudaStream_t st);

@@ -270,7 +270,7 @@ l16_kernel(const float *__restrict__ seq, const float *__restrict__ cb,
     cluster_sync();
 
     bool failed = false;
-    // Test-only fault injection (BCJR_B200_TEST_DROP_SENDS): CTA rank 1 never
+    // Test-only fault injection (BCJR_OPT_TEST_DROP_SENDS): CTA rank 1 never
     // sends its alpha-sweep outputs, so every consumer's bounded wait expires.
     const bool drop = drop_sends != 0 && rank == 1;
     uint32_t use[kSlots], hcnt[kSlots];   // ring consumptions / TMA row loads waited, per slot

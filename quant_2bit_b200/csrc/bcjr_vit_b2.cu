@@ -6,7 +6,8 @@
 //   cum_t(s) = m_t(s >> 2) + (c(s) - w_t)^2,   m_t(h) = min_p cum_{t-1}(p 2^14 + h),   m_0 = 0
 //
 // in fp32 with d = c - w, d * d and min + local each rounded (no fused
-// multiply-add), no renormalisation, the lowest p and the lowest final state
+// multiply-add: the sums are scalar __fadd_rn, add2_sep of bcjr_cluster.cuh,
+// which the compiler does not merge with the f32x2 products), no renormalisation, the lowest p and the lowest final state
 // on ties, so walks are bit-identical to the reference encoder's.
 //
 // Work decomposition.  With M = 14 the 2^16 states split into 4096
@@ -65,6 +66,7 @@ constexpr int kNMax = 512;
 struct alignas(128) Smem {
     float buf[kSlots][2][kIn];            // input ring: group minima of the previous step
     float tok[kSlots][2][kCL * kWarps];   // per-warp tokens riding with the data
+    float zero[kIn];                      // inputs of step 0 (m_0 = 0): plain loads, no selects
     float w[kSlots][kNMax];
     float wv[kSlots][kWarps];             // per-warp best final cost
     int wi[kSlots][kWarps];               // and its state
@@ -114,6 +116,7 @@ vit_b2_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
         }
     }
 
+    for (int i = tid; i < kIn; i += kNT) sm.zero[i] = 0.f;
     if (tid == 0) {
         for (int z = 0; z < kSlots; ++z)
             for (int x = 0; x < 2; ++x) mbar_init(sbase + soff(&sm.full[z][x]), 1);
@@ -153,7 +156,7 @@ vit_b2_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
 #pragma unroll
             for (int z = 0; z < kSlots; ++z) {
                 if (!active[z]) continue;
-                const float *in = nullptr;    // m_0 = 0: no inputs at step 0
+                const float *in = sm.zero;    // m_0 = 0
                 if (t > 0) {
                     const int x = use[z] & 1;
                     const uint32_t bar = sbase + soff(&sm.full[z][x]);
@@ -177,11 +180,11 @@ vit_b2_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
                     F2 x[4][2];                       // cum_t of my 16 states
 #pragma unroll
                     for (int p = 0; p < 4; ++p) {
-                        const F2 A = bc(in ? in[p * kRPC + rl] : 0.f);
+                        const F2 A = bc(in[p * kRPC + rl]);
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             const F2 d = sub2(C[j][p][h], W);
-                            x[p][h] = add2(A, mul2(d, d));
+                            x[p][h] = add2_sep(A, mul2(d, d));
                         }
                     }
                     float o[4];
@@ -193,10 +196,10 @@ vit_b2_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
 #pragma unroll
                         for (int p = 1; p < 4; ++p) {
                             const float v = (c & 1) ? x[p][c >> 1].y : x[p][c >> 1].x;
-                            if (v < m) { m = v; bi = (uint32_t)p; }
+                            if (v < m) { m = v; bi = (uint32_t)p << (2 * c); }
                         }
                         o[c] = m;
-                        packed |= bi << (2 * c);
+                        packed |= bi;
                     }
                     if (!last) {
                         bpt[rg[j]] = (unsigned char)packed;
@@ -358,6 +361,12 @@ long vit_b2_chunk(int B, int N) {
 bool vit_b2_applicable(int N, int L, int k, int V, const void *cb) {
     return L == vb2::kL && k == vb2::kB && V == 1 && N >= 1 && N <= vb2::kNMax &&
            (reinterpret_cast<uintptr_t>(cb) & 15u) == 0 && vit_b2_max_clusters() > 0;
+}
+
+int vit_b2_launches(int B, int N) {
+    if (B <= 0) return 0;
+    const long c = vit_b2_chunk(B, N);
+    return (int)(2 * ((B + c - 1) / c));
 }
 
 size_t vit_b2_workspace_bytes(int B, int N) {

@@ -119,7 +119,7 @@ vit_b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
     cluster_sync();
 
     bool failed = false;
-    // Test-only fault injection (BCJR_B200_TEST_DROP_SENDS): CTA rank 1 never
+    // Test-only fault injection (BCJR_OPT_TEST_DROP_SENDS): CTA rank 1 never
     // sends its group minima or tokens, so every consumer's bounded wait expires.
     const bool drop = drop_sends != 0 && rank == 1;
     uint32_t use[kSlots];
@@ -180,7 +180,8 @@ vit_b4_kernel(const float *__restrict__ seq, const float *__restrict__ cb, int B
                     for (int i = 0; i < 8; ++i) {
                         const F2 A = *reinterpret_cast<const F2 *>(in + 2 * (i * kRPC + rl));
                         const F2 d0 = sub2(C0[rr][i], W0), d1 = sub2(C1[rr][i], W1);
-                        x[i] = add2(A, add2(mul2(d0, d0), mul2(d1, d1)));   // cum_t of 16 states
+                        // cum_t of 16 states; separately rounded sums (add2_sep)
+                        x[i] = add2_sep(A, add2_sep(mul2(d0, d0), mul2(d1, d1)));
                     }
                     float m = x[0].x;
                     int bi = 0;
@@ -337,6 +338,10 @@ constexpr long kVitChunk = 2048;   // sequences per forward + backtrace launch p
 bool vit_b4_applicable(int N, int L, int k, int V, const void *cb) {
     return L == vb4::kL && k * V == vb4::kB && V == vb4::kV && N >= 1 && N <= vb4::kNMax &&
            (reinterpret_cast<uintptr_t>(cb) & 7u) == 0 && vit_b4_max_clusters() > 0;
+}
+
+int vit_b4_launches(int B) {
+    return B <= 0 ? 0 : (int)(2 * ((B + kVitChunk - 1) / kVitChunk));
 }
 
 size_t vit_b4_workspace_bytes(int B, int N) {

@@ -228,6 +228,14 @@ BCJR_API size_t bcjr_viterbi_workspace_bytes(int B, int N, int L, int k, int V) 
     return kVitHeader + need;
 }
 
+BCJR_API int bcjr_viterbi_launches(int B, int N, int L, int k, int V) {
+    const int st = vit_check(B, N, L, k, V);
+    if (st) return -st;
+    if (B == 0) return 0;
+    const int which = vit_cluster(N, L, k, V, nullptr);
+    return which == 4 ? bcjr::vit_b4_launches(B) : which == 2 ? bcjr::vit_b2_launches(B, N) : 1;
+}
+
 BCJR_API int bcjr_viterbi(const float *seq, const float *cb, int B, int N, int L, int k, int V,
                           int *bitstreams, int *start_states, float *recons, float *mses,
                           void *ws, size_t ws_bytes, bcjr_stream_t stream) {

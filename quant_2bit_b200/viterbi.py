@@ -9,6 +9,7 @@ There is no CPU path: CPU tensors raise.
 """
 import math
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -55,4 +56,23 @@ def viterbi_encode_v_batched_cuda(sequences, codebook, k=2):
     return viterbi_encode_batched(sequences, codebook.reshape(1 << L, V), L, k, V)
 
 
-__all__ = ["viterbi_encode_batched", "viterbi_encode_v_batched_cuda"]
+def viterbi_encode(sequence, L, k, decode_fn, return_trace=False):
+    """The V=1 encoder of src/viterbi/encode.py:47-90 (one sequence, numpy in
+    and out) on the sm_100a kernels: (bitstream int32 (T,), start_state int,
+    recon float32 (T,), mse float), bit-identical to the reference's for a
+    float32 sequence (its arithmetic is fp32 then).  decode_fn maps a uint32
+    array of states to their codewords, as in the reference.  The per-step
+    cost trace (return_trace=True) is not kept by the kernels."""
+    if return_trace:
+        raise NotImplementedError("return_trace: the kernels keep no per-step cost rows")
+    if not torch.cuda.is_available():
+        raise RuntimeError("the Viterbi kernel needs a CUDA device (there is no CPU path)")
+    states = np.arange(1 << L, dtype=np.uint32)
+    cb = torch.tensor(np.asarray(decode_fn(states), dtype=np.float32).reshape(1 << L, 1),
+                      device="cuda")
+    seq = torch.tensor(np.asarray(sequence, dtype=np.float32).reshape(1, -1), device="cuda")
+    bits, starts, recons, mses = viterbi_encode_batched(seq, cb, L, k, 1)
+    return (bits[0].cpu().numpy(), int(starts[0]), recons[0].cpu().numpy(), float(mses[0]))
+
+
+__all__ = ["viterbi_encode", "viterbi_encode_batched", "viterbi_encode_v_batched_cuda"]

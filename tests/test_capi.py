@@ -64,6 +64,14 @@ def test_shape_validation_without_gpu(lib):
     assert lib.bcjr_check_shape(0, 8, 16, 2, 1) == 0             # empty batch is valid
 
 
+def test_viterbi_launch_count_shape_checks(lib):
+    """bcjr_viterbi_launches: 0 for an empty batch, a negative status code
+    for a shape the encoder does not build (no device work either way)."""
+    assert lib.bcjr_viterbi_launches(0, 128, 16, 2, 2) == 0
+    assert lib.bcjr_viterbi_launches(4, 0, 16, 2, 1) == -1       # N = 0
+    assert lib.bcjr_viterbi_launches(4, 8, 16, 3, 2) == -2       # kV = 6
+
+
 def test_status_strings(lib):
     for code in range(0, 9):
         assert lib.bcjr_status_string(code).decode()

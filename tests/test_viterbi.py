@@ -90,6 +90,26 @@ def test_kernel_matches_oracle(cuda_ok, L, k, V, B, N, kind):
 
 
 @pytest.mark.gpu
+def test_v1_entry_point_matches_reference_encodes(cuda_ok):
+    """quant_2bit_b200.viterbi.viterbi_encode, the drop-in for the
+    reference's V=1 viterbi_encode (numpy in and out, a decode_fn), on the
+    reference's own encodes: bit-exact walks (L=16, k=2 on the cluster
+    kernel; the smaller trellises on the one-block kernel)."""
+    from quant_2bit_b200.viterbi import viterbi_encode
+    for name in [n for n in NAMES if "_V1_" in n]:
+        d, cb = _case(name)
+        for i in range(d["seqs"].shape[0]):
+            bits, start, rec, mse = viterbi_encode(d["seqs"][i], int(d["L"]), int(d["k"]),
+                                                   lambda s: cb[s, 0])
+            np.testing.assert_array_equal(bits, d["bits"][i])
+            assert start == int(d["starts"][i])
+            np.testing.assert_array_equal(rec, d["recons"][i])
+            np.testing.assert_allclose(mse, d["mses"][i], rtol=1e-6, atol=1e-7)
+    with pytest.raises(NotImplementedError):
+        viterbi_encode(np.zeros(8, np.float32), 16, 2, lambda s: cb[s, 0], return_trace=True)
+
+
+@pytest.mark.gpu
 def test_reference_entry_point_and_errors(cuda_ok):
     from quant_2bit_b200.viterbi import viterbi_encode_v_batched_cuda
     d, cb = _case("viterbi_L16_k2_V2_gauss.npz")
@@ -104,15 +124,18 @@ def test_reference_entry_point_and_errors(cuda_ok):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("V,B,N", [(2, 64, 128), (2, 2049, 8), (2, 3, 512),
-                                   (1, 64, 256), (1, 1000, 8), (1, 449, 512)])
+@pytest.mark.parametrize("V,B,N", [(2, 64, 128), (2, 2049, 8), (2, 3, 512), (2, 1024, 512),
+                                   (1, 64, 256), (1, 1000, 8), (1, 520, 512)])
 def test_cluster_and_generic_kernels_agree(cuda_ok, V, B, N):
     """L=16, k=2 runs on the 4-CTA cluster kernels (b = 4 at V=2, b = 2 at
     V=1); the test option BCJR_OPT_FORCE_GENERIC sends it to the
     one-block-per-sequence kernel.  Both are exact: identical results,
     across the chunking of the cluster paths (2048 sequences at V=2, whole
-    waves of at most 2^18 / N sequences at V=1: 449 x 512 takes two
-    chunks) and at the longest N they serve."""
+    waves of at most 2^18 / N sequences at V=1: 520 x 512 takes two
+    chunks) and at the longest N they serve.  The large batches hold
+    one-ulp near-ties between predecessors, where a fused multiply-add in
+    the costs (d*d rounded into the sum) takes another walk: 520 x 512 at
+    V=1 did until the sums were separately rounded."""
     from quant_2bit_b200 import _lib
     from quant_2bit_b200.viterbi import viterbi_encode_batched
     rng = np.random.default_rng(B + N + V)
@@ -126,6 +149,9 @@ def test_cluster_and_generic_kernels_agree(cuda_ok, V, B, N):
     for x, y in zip(a[:3], b[:3]):
         assert torch.equal(x, y)
     torch.testing.assert_close(a[3], b[3], rtol=1e-6, atol=1e-7)
+    # one launch pair (min-sum kernel, walk-back) per chunk on the cluster paths
+    chunks = {(2, 2049): 2, (1, 520): 2}.get((V, B), 1)
+    assert _lib.load().bcjr_viterbi_launches(B, N, 16, 2, V) == 2 * chunks
 
 
 @pytest.mark.gpu
