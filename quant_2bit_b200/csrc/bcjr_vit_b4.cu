@@ -45,7 +45,9 @@ constexpr int kNT = 512;
 constexpr int kWarps = kNT / 32;
 // Four sequences in flight per cluster: measured on B200 (4096 x 128)
 // 3.68e13 transitions/s with 2, 3.98e13 with 3, 4.28e13 with 4, 4.07e13
-// with 8 (shared memory ~13 KB per slot; 128 registers, no spills).
+// with 8 (shared memory ~13 KB per slot), with the costs' sums still fused
+// by the compiler; with the separately rounded sums (add2_sep) 3.66e13 at 4
+// (128 registers, an 8-byte spill).
 #ifndef BCJR_VIT_SLOTS
 #define BCJR_VIT_SLOTS 4
 #endif
