@@ -7,8 +7,9 @@
 //
 // in fp32 with d = c - w, d * d and min + local each rounded (no fused
 // multiply-add: the sums are scalar __fadd_rn, add2_sep of bcjr_cluster.cuh,
-// which the compiler does not merge with the f32x2 products), no renormalisation, the lowest p and the lowest final state
-// on ties, so walks are bit-identical to the reference encoder's.
+// which the compiler does not merge with the f32x2 products), no
+// renormalisation, the lowest p and the lowest final state on ties, so walks
+// are bit-identical to the reference encoder's.
 //
 // Work decomposition.  With M = 14 the 2^16 states split into 4096
 // butterflies r: states s = p 2^14 + 4 r + c, p, c in 0..3.  Butterfly r
