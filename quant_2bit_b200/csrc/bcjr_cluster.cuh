@@ -157,9 +157,10 @@ __device__ __forceinline__ F2 mul2(F2 a, F2 b) { return __fmul2_rn(a, b); }
 // Separately rounded sums for arithmetic that must equal the reference's
 // bit for bit (the hard Viterbi costs a + d*d).  The compiler merges an
 // f32x2 multiply and a following f32x2 add into one fused multiply-add, also
-// when both are written as inline PTX with an explicit .rn (measured on B200:
-// the costs then followed fma(d, d, a), and a one-ulp near-tie between two
-// predecessors took the other one); the scalar __fadd_rn is never merged.
+// when both are written as inline PTX with an explicit .rn and also under
+// -fmad=false (measured on B200: the costs then followed fma(d, d, a), and a
+// one-ulp near-tie between two predecessors took the other one); the scalar
+// __fadd_rn is never merged.
 __device__ __forceinline__ F2 add2_sep(F2 a, F2 b) {
     return mk(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
 }
