@@ -27,6 +27,35 @@ def test_oracle_matches_reference_encoder(name):
     np.testing.assert_allclose(mse, d["mses"], rtol=1e-6, atol=1e-7)
 
 
+def test_large_gpu_case_separates_fused_from_exact_costs():
+    """The 520 x 512 batch (V=1) of test_cluster_and_generic_kernels_agree
+    holds a one-ulp near-tie between two predecessors, so a kernel whose
+    costs a + d*d are one fused multiply-add instead of two roundings fails
+    that test: row 101's exact walk (the oracle) differs from the same
+    recursion with fma(d, d, a) (emulated in fp64: d*d is exact there)."""
+    B, N, V = 520, 512, 1
+    rng = np.random.default_rng(B + N + V)          # as the GPU test draws them
+    cb = rng.standard_normal((1 << 16, 1)).astype(np.float32)
+    seq = rng.standard_normal((B, V * N)).astype(np.float32)[101:102]
+    bits, starts, _, _ = viterbi.viterbi(seq, cb, 16, 2, 1)
+    c = cb[:, 0]
+    top = np.arange(1 << 16) >> 2
+    cum = np.zeros(1 << 16, np.float32)
+    bps = []
+    for t in range(N):
+        pc = cum.reshape(4, 1 << 14)
+        bps.append(pc.argmin(0))
+        d = (c - seq[0, t]).astype(np.float32).astype(np.float64)
+        cum = (pc.min(0)[top].astype(np.float64) + d * d).astype(np.float32)
+    s = int(np.argmin(cum))
+    walk = [s]
+    for t in range(N - 1, 0, -1):
+        s = (int(bps[t][s >> 2]) << 14) | (s >> 2)
+        walk.append(s)
+    fused_bits = np.array(walk[::-1]) & 3
+    assert not np.array_equal(fused_bits, bits[0])
+
+
 def test_oracle_walk_replays_to_its_reconstruction():
     """viterbi_decode (src/viterbi/encode.py:313-328): replaying the bitstream
     from the start state gives the reconstruction."""
